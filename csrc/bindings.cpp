@@ -1,0 +1,70 @@
+// Python bindings of the sm_100a kernel library (module openmini_v1_b200._C).
+#include <torch/extension.h>
+
+void om_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> resid,
+             c10::optional<torch::Tensor> workspace, torch::Tensor status, int64_t force_swap,
+             int64_t force_splits);
+std::vector<int64_t> om_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, bool allow_split);
+void om_gemm_wq(torch::Tensor x, torch::Tensor qweight, torch::Tensor scales, int64_t qtype, torch::Tensor out,
+                c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace, torch::Tensor status,
+                int64_t force_swap, int64_t force_splits);
+void om_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w, torch::Tensor out,
+                double eps);
+void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, torch::Tensor out,
+                  double eps);
+void om_silu_mul(torch::Tensor gu, torch::Tensor out);
+void om_gelu(torch::Tensor x, torch::Tensor y);
+void om_softmax(torch::Tensor x, torch::Tensor y, double scale);
+void om_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, torch::Tensor status);
+void om_rope_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor slots, torch::Tensor k_cache,
+                torch::Tensor v_cache, torch::Tensor inv_freq, int64_t Hq, int64_t Hkv, int64_t D, int64_t mode,
+                torch::Tensor status);
+void om_kv_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::Tensor k_cache,
+                 torch::Tensor v_cache);
+void om_paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                        torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor out, torch::Tensor workspace,
+                        int64_t Hq, int64_t max_ctx, double scale, torch::Tensor status);
+int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_t max_ctx);
+void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
+               torch::Tensor rng, torch::Tensor out_tok, c10::optional<torch::Tensor> out_logprob,
+               c10::optional<torch::Tensor> keep_mask);
+void om_repetition_penalty(torch::Tensor logits, torch::Tensor prev, torch::Tensor penalty);
+void om_decode_advance(torch::Tensor sampled, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx,
+                       torch::Tensor slots, torch::Tensor bt, torch::Tensor rng, c10::optional<torch::Tensor> hist,
+                       torch::Tensor step);
+void om_quantize_q4(torch::Tensor w, torch::Tensor q, torch::Tensor scales, c10::optional<torch::Tensor> scales_f16);
+void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out);
+void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale);
+void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "openmini_v1_b200 sm_100a kernels";
+  m.def("gemm", &om_gemm, "bf16 tcgen05 GEMM: out = x @ w^T (+ resid)", py::arg("x"), py::arg("w"),
+        py::arg("out"), py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
+        py::arg("force_swap") = -1, py::arg("force_splits") = 0);
+  m.def("gemm_plan", &om_gemm_plan);
+  m.def("gemm_wq", &om_gemm_wq, "weight-only quantised tcgen05 GEMM (0 = Q4 block-32, 1 = INT8 per row)",
+        py::arg("x"), py::arg("qweight"), py::arg("scales"), py::arg("qtype"), py::arg("out"),
+        py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
+        py::arg("force_swap") = -1, py::arg("force_splits") = 0);
+  m.def("rmsnorm", &om_rmsnorm, py::arg("x"), py::arg("delta"), py::arg("w"), py::arg("out"), py::arg("eps"));
+  m.def("layernorm", &om_layernorm);
+  m.def("silu_mul", &om_silu_mul);
+  m.def("gelu", &om_gelu);
+  m.def("softmax", &om_softmax);
+  m.def("embedding", &om_embedding);
+  m.def("rope_kv", &om_rope_kv);
+  m.def("kv_write", &om_kv_write);
+  m.def("paged_attention", &om_paged_attention);
+  m.def("paged_attention_workspace", &om_paged_attention_workspace);
+  m.def("sample", &om_sample, py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("top_k"),
+        py::arg("rng"), py::arg("out_tok"), py::arg("out_logprob") = py::none(),
+        py::arg("keep_mask") = py::none());
+  m.def("repetition_penalty", &om_repetition_penalty);
+  m.def("decode_advance", &om_decode_advance);
+  m.def("quantize_q4", &om_quantize_q4, py::arg("w"), py::arg("q"), py::arg("scales"),
+        py::arg("scales_f16") = py::none());
+  m.def("dequant_q4", &om_dequant_q4);
+  m.def("quantize_int8", &om_quantize_int8);
+  m.def("dequant_int8", &om_dequant_int8);
+}

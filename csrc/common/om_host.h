@@ -1,0 +1,59 @@
+// Host helpers shared by the extension's .cu files: error checks, SM count,
+// TMA tensor-map encoding through the driver entry point (so the extension
+// does not link libcuda directly and still imports on a machine without a GPU).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <mutex>
+
+#define OM_CUDA_CHECK(x)                                                                   \
+  do {                                                                                     \
+    cudaError_t _e = (x);                                                                  \
+    TORCH_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " at ", __FILE__, \
+                ":", __LINE__);                                                            \
+  } while (0)
+
+namespace om {
+
+inline int num_sms(int dev = -1) {
+  static int cache[64] = {0};
+  if (dev < 0) OM_CUDA_CHECK(cudaGetDevice(&dev));
+  if (cache[dev] == 0) OM_CUDA_CHECK(cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev));
+  return cache[dev];
+}
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    OM_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major 2-D tensor [outer, inner] with row stride `ld` elements.
+inline CUtensorMap make_tmap_2d(const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                                uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
+                                CUtensorMapSwizzle sw) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((strides[0] & 15) == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUresult r = encode_fn()(&m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+}  // namespace om

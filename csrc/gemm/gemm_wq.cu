@@ -1,0 +1,126 @@
+// Host launcher of the weight-only-quantised tcgen05 GEMM (Q4 block-32 / INT8 per row).
+#include "../common/om_host.h"
+#include "gemm_launch.h"
+#include "gemm_wq.cuh"
+
+namespace om {
+
+template <int BX, int QT, bool SWAP>
+static void launch_wq(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, const GemmArgs& g,
+                      int grid, cudaStream_t st) {
+  using C = WqCfg<BX, QT>;
+  static bool attr_set[64] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    OM_CUDA_CHECK(cudaFuncSetAttribute(gemm_wq_tc_kernel<BX, QT, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  gemm_wq_tc_kernel<BX, QT, SWAP><<<grid, 512, C::SMEM_BYTES, st>>>(tx, tq, ts, g);
+  OM_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int QT>
+static void dispatch(int bx, bool swap, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
+                     const GemmArgs& g, int grid, cudaStream_t st) {
+  if (!swap) return launch_wq<128, QT, false>(tx, tq, ts, g, grid, st);
+  switch (bx) {
+    case 32: return launch_wq<32, QT, true>(tx, tq, ts, g, grid, st);
+    case 64: return launch_wq<64, QT, true>(tx, tq, ts, g, grid, st);
+    case 128: return launch_wq<128, QT, true>(tx, tq, ts, g, grid, st);
+    default: return launch_wq<256, QT, true>(tx, tq, ts, g, grid, st);
+  }
+}
+
+}  // namespace om
+
+// qtype 0: Q4 (qweight uint8 [N, K/2], scales bf16 [K/32, N]); 1: INT8 (qweight int8 [N, K], scales fp32 [N])
+void om_gemm_wq(torch::Tensor x, torch::Tensor qweight, torch::Tensor scales, int64_t qtype, torch::Tensor out,
+                c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace, torch::Tensor status,
+                int64_t force_swap, int64_t force_splits) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_wq: x");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1, "gemm_wq: out");
+  const int M = x.size(0), K = x.size(1), N = qweight.size(0);
+  TORCH_CHECK(K % 64 == 0, "gemm_wq: K must be a multiple of 64");
+  TORCH_CHECK(qweight.is_contiguous() && scales.is_contiguous(), "gemm_wq: packed weight contiguous");
+  if (qtype == 0) {
+    TORCH_CHECK(qweight.size(1) == K / 2 && scales.scalar_type() == at::kBFloat16 && scales.size(0) == K / 32 &&
+                    scales.size(1) == N && N % 8 == 0,
+                "gemm_wq: Q4 layout");
+  } else {
+    TORCH_CHECK(qweight.size(1) == K && scales.scalar_type() == at::kFloat && scales.numel() == N, "gemm_wq: I8");
+  }
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_wq: out shape");
+  if (M == 0) return;
+  const int sms = om::num_sms();
+  const bool swap = force_swap >= 0 ? force_swap != 0 : M <= 256;
+  TORCH_CHECK(!swap || M <= 256, "gemm_wq: swap mode needs M <= 256");
+  const int rows = swap ? N : M, cols = swap ? M : N;
+  const int bx = swap ? (M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256) : 128;
+  const int bn_mma = swap ? bx : 128;
+  om::GemmArgs g;
+  g.rows = rows;
+  g.cols = cols;
+  g.tiles_r = (rows + 127) / 128;
+  g.tiles_c = (cols + bn_mma - 1) / bn_mma;
+  g.num_kb = K / 64;
+  const int units = g.tiles_r * g.tiles_c;
+  int splits = 1;
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (workspace.has_value()) {
+    ws = workspace->data_ptr<float>();
+    ws_bytes = workspace->numel() * sizeof(float);
+  }
+  if (ws && N % 4 == 0) {
+    if (force_splits > 0)
+      splits = (int)force_splits;
+    else if (units < sms)
+      splits = std::max(1, sms / units);
+    splits = std::min<int>(splits, g.num_kb);
+    splits = std::min<int>(splits, (int)std::max<size_t>(1, ws_bytes / ((size_t)M * N * sizeof(float))));
+  }
+  const int kbps = (g.num_kb + splits - 1) / splits;
+  splits = (g.num_kb + kbps - 1) / kbps;
+  g.splits = splits;
+  g.kb_per_split = kbps;
+  g.swap = swap ? 1 : 0;
+  g.status = status.data_ptr<int>();
+  g.ldo = out.stride(0);
+  g.wscale = qtype == 1 ? scales.data_ptr<float>() : nullptr;
+  const __nv_bfloat16* rp = resid.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
+  if (resid.has_value())
+    TORCH_CHECK(resid->sizes() == out.sizes() && resid->stride(0) == out.stride(0), "gemm_wq: resid layout");
+  if (splits > 1) {
+    g.epi = om::EPI_PARTIAL;
+    g.out = ws;
+    g.resid = nullptr;
+  } else {
+    g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
+    g.out = out.data_ptr();
+    g.resid = rp;
+  }
+  CUtensorMap tx = om::make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, x.stride(0), 64, bx,
+                                    CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tq, ts;
+  if (qtype == 0) {
+    tq = om::make_tmap_2d(qweight.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, K / 2, 32, 128,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+    ts = om::make_tmap_2d(scales.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K / 32, N, 128, 2,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    tq = om::make_tmap_2d(qweight.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, K, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+    ts = tq;
+  }
+  const int grid = std::min(units * splits, sms);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  if (qtype == 0)
+    om::dispatch<om::WQ_Q4>(bx, swap, tx, tq, ts, g, grid, st);
+  else
+    om::dispatch<om::WQ_I8>(bx, swap, tx, tq, ts, g, grid, st);
+  if (splits > 1)
+    om::launch_splitk_reduce(ws, splits, M, N, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rp,
+                             qtype == 1 ? scales.data_ptr<float>() : nullptr, st);
+}
