@@ -1,0 +1,56 @@
+"""Mixture-of-experts FFN: router -> top-k -> softmax over the k logits ->
+SwiGLU experts -> weighted combine.
+
+Routing follows the reference's top_k_selection (top-k first, then softmax over
+the selected logits; openmini-server/src/model/inference/model.rs:1325 and
+813-960). Keep-Routing replay (openmini-server/src/rl/keep_routing.rs:113-180)
+is supported by ``ForwardBatch.forced_routing[layer] = expert ids [T, k]``:
+the forward then uses those experts (weights recomputed from the current
+router so gradients still flow), and ``record_routing`` captures the ids the
+router chose.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+
+
+def route(router_logits: torch.Tensor, k: int, forced: torch.Tensor | None = None):
+    """Returns (expert ids [T, k] int64, weights [T, k] fp32)."""
+    lg = router_logits.float()
+    if forced is not None:
+        ids = forced.long()
+        sel = lg.gather(1, ids)
+    else:
+        sel, ids = torch.topk(lg, k, dim=-1)
+    w = torch.softmax(sel, dim=-1)
+    return ids, w
+
+
+def moe_forward(model, layer_idx, L, x, fb):
+    cfg = model.cfg.moe
+    T, D = x.shape
+    logits = ops.linear(x, L["router"])
+    forced = fb.forced_routing.get(layer_idx) if fb.forced_routing else None
+    ids, w = route(logits, cfg.top_k, forced)
+    if fb.record_routing is not None:
+        fb.record_routing[layer_idx] = ids.to(torch.int32)
+    out = torch.zeros(T, D, dtype=torch.float32, device=x.device)
+    flat = ids.reshape(-1)
+    tok = torch.arange(T, device=x.device).repeat_interleave(cfg.top_k)
+    wt = w.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    counts = torch.bincount(flat, minlength=cfg.num_experts).tolist()
+    start = 0
+    for e, n in enumerate(counts):
+        if n == 0:
+            continue
+        sel = order[start:start + n]
+        start += n
+        t_idx = tok[sel]
+        xe = x.index_select(0, t_idx)
+        gu = ops.linear(xe, L["experts_gate_up"][e])
+        y = ops.linear(ops.silu_mul(gu), L["experts_down"][e])
+        out.index_add_(0, t_idx, y.float() * wt[sel, None])
+    return out.to(x.dtype)

@@ -1,0 +1,240 @@
+"""Numerics of every sm_100a kernel against the plain PyTorch fp32 statement
+of the same op (``openmini_v1_b200.ops.reference``), seeded random inputs."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from openmini_v1_b200 import _native, ops
+from openmini_v1_b200.models.quantize import Int8Weight, Q4Weight
+from openmini_v1_b200.ops import reference as ref
+
+DEV = "cuda"
+
+
+def _rand(*shape, dtype=torch.bfloat16, std=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * std).to(dtype)
+
+
+def _close(a, b, rtol=2e-2, atol=2e-2):
+    a, b = a.float(), b.float()
+    err = (a - b).abs()
+    tol = atol + rtol * b.abs()
+    bad = (err > tol).float().mean().item()
+    assert bad < 1e-3, f"max err {err.max().item():.4g}, frac bad {bad:.4g}"
+
+
+def test_native_loaded():
+    assert _native.have_C()
+    assert "openmini_v1_b200" in _native.C().__file__
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (7, 1280, 8192), (32, 10240, 8192), (64, 2000, 520),
+                                   (128, 512, 256), (129, 384, 192), (300, 1000, 520), (1024, 2048, 4096),
+                                   (2048, 4096, 1024)])
+def test_gemm(M, N, K):
+    x = _rand(M, K, seed=1)
+    w = _rand(N, K, std=0.05, seed=2)
+    y = ops.linear(x, w)
+    torch.cuda.synchronize()
+    ops.check_status()
+    _close(y, ref.linear(x, w))
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 4096, 4096), (512, 1024, 2048)])
+def test_gemm_residual_inplace(M, N, K):
+    x = _rand(M, K, seed=3)
+    w = _rand(N, K, std=0.05, seed=4)
+    h = _rand(M, N, seed=5)
+    expect = ref.linear(x, w, h)
+    ops.linear(x, w, out=h, resid=h)
+    torch.cuda.synchronize()
+    _close(h, expect)
+
+
+@pytest.mark.parametrize("swap,splits", [(0, 1), (1, 1), (1, 4), (0, 3)])
+def test_gemm_forced_paths(swap, splits):
+    M, N, K = 96, 768, 1024
+    x = _rand(M, K, seed=6)
+    w = _rand(N, K, std=0.05, seed=7)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    c = ops.ctx(DEV)
+    _native.C().gemm(x, w, out, None, c.workspace("gemm", 1 << 24), c.status, swap, splits)
+    torch.cuda.synchronize()
+    _close(out, ref.linear(x, w))
+
+
+def test_quantize_roundtrip_matches_reference():
+    w = _rand(256, 512, std=0.02, seed=8)
+    q = Q4Weight.from_dense(w)
+    qr, sr = ref.quantize_q4(w.cpu())
+    assert torch.equal(q.qweight.cpu(), qr)
+    assert torch.equal(q.scales_t.t().cpu(), sr)
+    assert torch.equal(q.dequantize().cpu(), ref.dequant_q4(qr, sr))
+    i8 = Int8Weight.from_dense(w)
+    q8, s8 = ref.quantize_int8(w.cpu())
+    assert (i8.qweight.cpu().int() - q8.int()).abs().max() <= 1
+    torch.testing.assert_close(i8.scale.cpu(), s8)
+
+
+@pytest.mark.parametrize("kind", ["q4", "int8"])
+@pytest.mark.parametrize("M,N,K", [(1, 1280, 8192), (32, 10240, 1024), (64, 1024, 4096), (100, 768, 512),
+                                   (256, 2048, 1024), (300, 1024, 2048), (1024, 4096, 1024)])
+def test_gemm_weight_only_quant(kind, M, N, K):
+    w = _rand(N, K, std=0.02, seed=9)
+    qw = Q4Weight.from_dense(w) if kind == "q4" else Int8Weight.from_dense(w)
+    x = _rand(M, K, seed=10)
+    y = qw.linear(x)
+    torch.cuda.synchronize()
+    ops.check_status()
+    _close(y, ref.linear(x, qw.dequantize()))
+    h = _rand(M, N, seed=11)
+    expect = ref.linear(x, qw.dequantize(), h)
+    qw.linear(x, out=h, resid=h)
+    torch.cuda.synchronize()
+    _close(h, expect)
+
+
+@pytest.mark.parametrize("D", [256, 4096, 8192])
+def test_rmsnorm(D):
+    x = _rand(37, D, seed=8)
+    w = _rand(D, seed=9) + 1
+    _close(ops.rmsnorm(x, w, 1e-5), ref.rmsnorm(x, w, 1e-5))
+    d = _rand(37, D, seed=10)
+    x2, x3 = x.clone(), x.clone()
+    y = ops.rmsnorm(x2, w, 1e-5, delta=d)
+    yr = ref.rmsnorm(x3, w, 1e-5, delta=d)
+    _close(x2, x3, 1e-2, 1e-2)
+    _close(y, yr)
+
+
+def test_act_norm_misc():
+    gu = _rand(33, 2 * 688, seed=11)
+    _close(ops.silu_mul(gu), ref.silu_mul(gu))
+    x = _rand(17, 1024, seed=12)
+    _close(ops.gelu(x), ref.gelu(x))
+    w, b = _rand(1024, seed=13), _rand(1024, seed=14)
+    _close(ops.layernorm(x, w, b, 1e-5), ref.layernorm(x, w, b, 1e-5))
+    _close(ops.softmax(x, 0.5), ref.softmax(x, 0.5), 1e-3, 1e-5)
+    table = _rand(1000, 256, seed=15)
+    ids = torch.randint(0, 1000, (50,), device=DEV, dtype=torch.int32)
+    assert torch.equal(ops.embedding(ids, table), ref.embedding(ids, table))
+
+
+def _paged_setup(S, Hkv, D, lens, nb, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    kc = _rand(nb, Hkv, 16, D, seed=seed + 1)
+    vc = _rand(nb, Hkv, 16, D, seed=seed + 2)
+    mb = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.zeros(S, mb, dtype=torch.int32)
+    o = 0
+    for s, l in enumerate(lens):
+        n = (l + 15) // 16
+        bt[s, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    return kc, vc, bt.to(DEV)
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(8, 1, 128), (4, 2, 64), (32, 32, 128), (40, 8, 128), (64, 8, 128)])
+def test_paged_attention_decode(Hq, Hkv, D):
+    lens = [1, 17, 300, 513, 1500, 2049] if Hq <= 40 else [1, 17, 300, 2049]
+    S = len(lens)
+    kc, vc, bt = _paged_setup(S, Hkv, D, lens, 400, seed=20)
+    q = _rand(S, Hq, D, seed=21)
+    rseq = torch.arange(S, dtype=torch.int32, device=DEV)
+    rctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(D)
+    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, scale, max_ctx=4096)
+    torch.cuda.synchronize()
+    ops.check_status()
+    _close(o.view(S, Hq, D), ref.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, scale))
+
+
+def test_paged_attention_prefill_rows():
+    Hq, Hkv, D = 8, 2, 128
+    L = 700
+    kc, vc, bt = _paged_setup(1, Hkv, D, [L], 64, seed=30)
+    q = _rand(L, Hq, D, seed=31)
+    rseq = torch.zeros(L, dtype=torch.int32, device=DEV)
+    rctx = torch.arange(1, L + 1, dtype=torch.int32, device=DEV)
+    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, 0.088, max_ctx=L)
+    torch.cuda.synchronize()
+    _close(o.view(L, Hq, D), ref.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, 0.088))
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_rope_kv(mode):
+    T, Hq, Hkv, D = 40, 8, 2, 128
+    qkv = _rand(T, (Hq + 2 * Hkv) * D, seed=40)
+    pos = torch.randint(0, 100000, (T,), dtype=torch.int32, device=DEV)
+    slots = torch.randperm(64 * 16, device=DEV)[:T].to(torch.int32)
+    slots[3] = -1
+    kc = torch.zeros(64, Hkv, 16, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    inv = ref.inv_freq(D, 500000.0).to(DEV)
+    q1 = qkv.clone()
+    ops.rope_kv(q1, pos, slots, kc, vc, inv, Hq, Hkv, D, mode)
+    q2 = qkv.clone()
+    ref.rope_kv(q2, pos, slots, kc2, vc2, inv, Hq, Hkv, D, mode)
+    torch.cuda.synchronize()
+    _close(q1, q2, 1e-2, 1e-2)
+    _close(kc, kc2, 1e-2, 1e-2)
+    assert torch.equal(vc, vc2)
+
+
+def test_sampler_greedy_and_topk1():
+    B, V = 8, 128256
+    lg = _rand(B, V, seed=50) * 3
+    z = torch.zeros(B, device=DEV)
+    tok, lp, _ = ops.sample(lg, z, torch.ones(B, device=DEV), torch.zeros(B, dtype=torch.int32, device=DEV),
+                            torch.zeros(B, 2, dtype=torch.int64, device=DEV))
+    assert torch.equal(tok.long(), lg.float().argmax(-1))
+    tok2, _, _ = ops.sample(lg, torch.full((B,), 0.7, device=DEV), torch.ones(B, device=DEV),
+                            torch.ones(B, dtype=torch.int32, device=DEV),
+                            torch.randint(0, 1 << 40, (B, 2), device=DEV))
+    assert torch.equal(tok2.long(), lg.float().argmax(-1))
+
+
+def test_sampler_matches_reference():
+    B, V = 6, 32000
+    lg = _rand(B, V, seed=51, dtype=torch.float32) * 2
+    temp = torch.tensor([0.7, 1.0, 0.5, 1.3, 0.7, 0.9], device=DEV)
+    top_p = torch.tensor([0.9, 0.5, 1.0, 0.95, 0.3, 0.8], device=DEV)
+    top_k = torch.tensor([0, 50, 20, 0, 0, 1000], dtype=torch.int32, device=DEV)
+    rng = torch.tensor([[11, 0], [12, 5], [13, 7], [14, 1], [15, 2], [16, 3]], dtype=torch.int64, device=DEV)
+    tok, lp, mask = ops.sample(lg, temp, top_p, top_k, rng, want_mask=True)
+    rt, rlp, rm = ref.sample(lg.cpu(), temp.cpu(), top_p.cpu(), top_k.cpu(), rng.cpu())
+    gm = ref.unpack_mask(mask.cpu(), V)
+    diff = (gm ^ rm).sum(-1)  # kept sets equal up to float-summation order at the cut-off
+    assert int(diff.max()) <= 2, diff
+    assert (tok.cpu() == rt).float().mean() >= 5 / 6
+    torch.testing.assert_close(lp.cpu(), rlp, rtol=1e-3, atol=1e-3)
+    for b in range(B):
+        assert gm[b, int(tok[b])]
+
+
+def test_sampler_distribution():
+    V = 64
+    lg = torch.full((1, V), -30.0, device=DEV)
+    lg[0, :4] = torch.log(torch.tensor([0.1, 0.2, 0.3, 0.4], device=DEV))
+    n = 4000
+    lgb = lg.expand(n, V).contiguous()
+    rng = torch.stack([torch.arange(n, device=DEV), torch.zeros(n, dtype=torch.int64, device=DEV)], 1).contiguous()
+    tok, _, _ = ops.sample(lgb, torch.ones(n, device=DEV), torch.ones(n, device=DEV),
+                           torch.zeros(n, dtype=torch.int32, device=DEV), rng)
+    freq = torch.bincount(tok.long().cpu(), minlength=V)[:4].float() / n
+    assert torch.allclose(freq, torch.tensor([0.1, 0.2, 0.3, 0.4]), atol=0.03), freq
+
+
+def test_repetition_penalty():
+    lg = _rand(2, 1000, seed=60, dtype=torch.float32)
+    prev = torch.tensor([[1, 5, 5, -1], [7, 8, 9, 10]], dtype=torch.int32, device=DEV)
+    pen = torch.tensor([1.3, 0.8], device=DEV)
+    a = ops.repetition_penalty(lg.clone(), prev, pen)
+    b = ref.repetition_penalty(lg.clone().cpu(), prev.cpu(), pen.cpu())
+    torch.testing.assert_close(a.cpu(), b)
