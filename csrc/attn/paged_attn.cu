@@ -206,9 +206,9 @@ static void launch_d(const AttnArgs& a, int rows, int G, cudaStream_t st) {
     case 16: paged_attn_kernel<D, 16><<<grid, 128, 0, st>>>(a); break;
     default: TORCH_CHECK(false, "paged_attention: unsupported GQA group ", G);
   }
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
   attn_merge_kernel<D><<<dim3(rows, a.Hq), 128, 0, st>>>(a);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 }  // namespace om

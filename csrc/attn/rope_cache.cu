@@ -89,7 +89,7 @@ void om_rope_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor slots,
       slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), inv_freq.data_ptr<float>(), Hq, Hkv, D, mode,
       k_cache.size(0) * 16, status.data_ptr<int>());
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_kv_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::Tensor k_cache,
@@ -102,5 +102,5 @@ void om_kv_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::T
       reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()),
       k.stride(0), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), Hkv, D);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }

@@ -37,7 +37,10 @@ void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out);
 void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale);
 void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
 
+#include "common/om_host.h"
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("launch_count", [] { return (int64_t)om::g_launches.load(); }, "kernel launches issued so far");
   m.doc() = "openmini_v1_b200 sm_100a kernels";
   m.def("gemm", &om_gemm, "bf16 tcgen05 GEMM: out = x @ w^T (+ resid)", py::arg("x"), py::arg("w"),
         py::arg("out"), py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),

@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <atomic>
 #include <mutex>
 
 #define OM_CUDA_CHECK(x)                                                                   \
@@ -16,7 +17,18 @@
                 ":", __LINE__);                                                            \
   } while (0)
 
+// Check the last launch and count it.
+#define OM_LAUNCH_CHECK()                  \
+  do {                                     \
+    OM_CUDA_CHECK(cudaGetLastError());     \
+    om::g_launches.fetch_add(1);           \
+  } while (0)
+
 namespace om {
+
+// Host-side count of kernel launches issued by this library (also counts
+// launches recorded into a CUDA graph during capture).
+inline std::atomic<long long> g_launches{0};
 
 inline int num_sms(int dev = -1) {
   static int cache[64] = {0};

@@ -48,7 +48,7 @@ static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     attr_set[dev] = true;
   }
   gemm_bf16_tc_kernel<BN><<<grid, 256, C::SMEM_BYTES, st>>>(ta, tb, g);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 GemmPlan plan_gemm(int M, int N, int K, int sms, bool allow_split, int force_swap) {
@@ -140,7 +140,7 @@ void launch_splitk_reduce(const float* ws, int splits, int M, int N, __nv_bfloat
   const size_t work = (size_t)M * (N / 4);
   const int blocks = (int)std::min<size_t>((work + nthreads - 1) / nthreads, (size_t)num_sms() * 8);
   splitk_reduce_kernel<<<blocks, nthreads, 0, st>>>(ws, splits, M, N, out, ldo, resid, col_scale);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 }  // namespace om

@@ -18,7 +18,7 @@ static void launch_wq(const CUtensorMap& tx, const CUtensorMap& tq, const CUtens
     attr_set[dev] = true;
   }
   gemm_wq_tc_kernel<BX, QT, SWAP><<<grid, 512, C::SMEM_BYTES, st>>>(tx, tq, ts, g);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 template <int QT>

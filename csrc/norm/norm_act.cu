@@ -252,7 +252,7 @@ void om_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tens
     rmsnorm_kernel<128, 4><<<T, 128, 0, st>>>(xp, dp, wp, op, D, ldx, ldd, ldo, (float)eps);
   else
     rmsnorm_kernel<256, 8><<<T, 256, 0, st>>>(xp, dp, wp, op, D, ldx, ldd, ldo, (float)eps);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, torch::Tensor out,
@@ -267,7 +267,7 @@ void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor>
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
       b.has_value() ? reinterpret_cast<const __nv_bfloat16*>(b->data_ptr()) : nullptr,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, (float)eps);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_silu_mul(torch::Tensor gu, torch::Tensor out) {
@@ -281,7 +281,7 @@ void om_silu_mul(torch::Tensor gu, torch::Tensor out) {
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms() * 16);
   silu_mul_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, F);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_gelu(torch::Tensor x, torch::Tensor y) {
@@ -292,7 +292,7 @@ void om_gelu(torch::Tensor x, torch::Tensor y) {
   const int blocks = (int)std::min<size_t>((n8 + 255) / 256, (size_t)num_sms() * 16);
   gelu_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), n8);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_softmax(torch::Tensor x, torch::Tensor y, double scale) {
@@ -303,7 +303,7 @@ void om_softmax(torch::Tensor x, torch::Tensor y, double scale) {
   if (T == 0) return;
   softmax_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), y.data_ptr<float>(), D, (float)scale);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, torch::Tensor status) {
@@ -315,5 +315,5 @@ void om_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, tor
   embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, table.size(0), status.data_ptr<int>());
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }

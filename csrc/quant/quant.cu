@@ -124,7 +124,7 @@ void om_quantize_q4(torch::Tensor w, torch::Tensor q, torch::Tensor scales, c10:
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), q.data_ptr<uint8_t>(),
       reinterpret_cast<__nv_bfloat16*>(scales.data_ptr()),
       scales_f16.has_value() ? reinterpret_cast<__half*>(scales_f16->data_ptr()) : nullptr, nb);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out) {
@@ -136,7 +136,7 @@ void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out) {
   om::dequant_q4_kernel<<<grid_for(nb), 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       q.data_ptr<uint8_t>(), reinterpret_cast<const __nv_bfloat16*>(scales.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nb);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale) {
@@ -145,7 +145,7 @@ void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale) {
   if (N == 0) return;
   om::quantize_int8_kernel<<<N, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), q.data_ptr<int8_t>(), scale.data_ptr<float>(), K);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out) {
@@ -154,5 +154,5 @@ void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out) {
   om::dequant_int8_kernel<<<grid_for(n), 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       q.data_ptr<int8_t>(), scale.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), q.size(1),
       n);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }

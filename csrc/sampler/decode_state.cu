@@ -49,5 +49,5 @@ void om_decode_advance(torch::Tensor sampled, torch::Tensor ids, torch::Tensor p
                                                 ctx.data_ptr<int>(), slots.data_ptr<int>(), bt.data_ptr<int>(),
                                                 bt.stride(0), rng.data_ptr<int64_t>(), hp, step.data_ptr<int>(), B,
                                                 hs);
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }

@@ -272,7 +272,7 @@ void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor to
     om::sample_kernel<__nv_bfloat16><<<B, om::SNT, 0, st>>>(a);
   else
     TORCH_CHECK(false, "sample: logits must be fp32 or bf16");
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }
 
 void om_repetition_penalty(torch::Tensor logits, torch::Tensor prev, torch::Tensor penalty) {
@@ -287,5 +287,5 @@ void om_repetition_penalty(torch::Tensor logits, torch::Tensor prev, torch::Tens
     om::rep_penalty_kernel<__nv_bfloat16><<<B, 256, 0, st>>>(
         reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0), V, prev.data_ptr<int>(),
         prev.size(1), penalty.data_ptr<float>());
-  OM_CUDA_CHECK(cudaGetLastError());
+  OM_LAUNCH_CHECK();
 }

@@ -210,7 +210,7 @@ class LLMEngine:
         chunks = so.chunks
         S = len(chunks)
         T = sum(c.end - c.start for c in chunks)
-        mb = self.max_blocks_per_seq if so.kind == "decode" else max(1, max((c.end + 15) // 16 for c in chunks))
+        mb = self.max_blocks_per_seq
         nL = sum(1 for c in chunks if c.wants_logits)
         n_i32 = 5 * T + S * mb + nL
         st = self.stage

@@ -53,8 +53,9 @@ class CollectiveOps:
         if self.size == 1:
             return t
         t = t.contiguous()
-        out = torch.empty((self.size,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t, group=self.group)
+        flat = torch.empty((self.size * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(flat, t, group=self.group)
+        out = flat.view((self.size,) + tuple(t.shape))
         dim = dim % t.dim()
         if dim == 0:
             return out.reshape((-1,) + tuple(t.shape[1:]))
