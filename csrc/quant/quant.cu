@@ -40,8 +40,9 @@ __global__ void quantize_q4_kernel(const __nv_bfloat16* __restrict__ w, uint8_t*
     uint8_t* dst = q + b * 16;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      int lo = (int)floorf(v[i] * id + 8.5f);
-      int hi = (int)floorf(v[i + 16] * id + 8.5f);
+      // separate multiply and add roundings (no FMA contraction) so the host quantiser matches bit for bit
+      int lo = (int)floorf(__fadd_rn(__fmul_rn(v[i], id), 8.5f));
+      int hi = (int)floorf(__fadd_rn(__fmul_rn(v[i + 16], id), 8.5f));
       lo = min(15, max(0, lo));
       hi = min(15, max(0, hi));
       dst[i] = (uint8_t)(lo | (hi << 4));
