@@ -258,3 +258,104 @@ int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_
   const int64_t np = std::max<int64_t>(1, (max_ctx + om::ATT_PART - 1) / om::ATT_PART);
   return rows * Hq * np * (D + 2);
 }
+
+// ============================================================================
+// Allocation-free C entry point for paged attention.
+//
+// This entry point has no counterpart in the reference. It exists for callers
+// that must not allocate device memory: code running inside a custom memory
+// pool or allocator hook, plugins hosted by another runtime that owns all
+// device memory, or real-time paths where a cudaMalloc could block or fail at
+// the wrong moment. Such callers pass only their inputs and outputs; the
+// split-KV partial results live in a fixed device array owned by this library.
+//
+// Limits and behaviour:
+//   * The scratch array holds OM_NOALLOC_SCRATCH_FLOATS fp32 values (16 MiB).
+//     A call needs rows * Hq * ceil(max_ctx / 512) * (head_dim + 2) floats and
+//     is rejected with OM_NOALLOC_TOO_LARGE if that exceeds the array.
+//   * Every GPU that loads this library reserves the 16 MiB until the process
+//     exits.
+//   * The first call on a device looks up the array's device address
+//     (cudaGetSymbolAddress with that device current) and caches it; make that
+//     first call before any stream capture.
+//   * All calls share the one array, which keeps the previous call's contents.
+//     Calls whose kernels overlap on the GPU (different streams, or several
+//     host threads) race on it; serialise them. Nothing in it needs clearing:
+//     every partial the merge kernel reads is written earlier in the same call.
+//   * No cudaMalloc / cudaFree or allocating library routine is called.
+// ============================================================================
+#include <mutex>
+
+#define OM_NOALLOC_SCRATCH_FLOATS (4u << 20)
+
+static __device__ __align__(256) float om_noalloc_scratch[OM_NOALLOC_SCRATCH_FLOATS];
+
+enum : int {
+  OM_NOALLOC_OK = 0,
+  OM_NOALLOC_TOO_LARGE = 1,   // request exceeds the fixed scratch array
+  OM_NOALLOC_BAD_ARGS = 2,    // unsupported head_dim / GQA group / null pointer
+  OM_NOALLOC_CUDA_ERROR = 3,  // symbol lookup or kernel launch failed
+};
+
+static float* om_noalloc_scratch_ptr() {
+  static std::mutex mu;
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, om_noalloc_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  return ptrs[dev];
+}
+
+// q [rows, Hq, D] bf16 (row stride q_ld elements), caches [num_blocks, Hkv, 16, D]
+// bf16, block_tables [S, max_blocks] int32, row_seq / row_ctx [rows] int32,
+// out [rows, Hq, D] bf16 (row stride out_ld). status may be null.
+// Returns an OM_NOALLOC_* code.
+extern "C" int om_paged_attention_noalloc(const void* q, int q_ld, const void* k_cache, const void* v_cache,
+                                          int num_blocks, int Hkv, int head_dim, const int* block_tables,
+                                          int max_blocks, const int* row_seq, const int* row_ctx, int rows,
+                                          void* out, int out_ld, int Hq, int max_ctx, float scale, int* status,
+                                          cudaStream_t stream) {
+  if (rows <= 0) return OM_NOALLOC_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !row_seq || !row_ctx || !out) return OM_NOALLOC_BAD_ARGS;
+  if (Hkv <= 0 || Hq % Hkv != 0 || (head_dim != 64 && head_dim != 128) || max_ctx <= 0) return OM_NOALLOC_BAD_ARGS;
+  const int G = Hq / Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 5 && G != 8 && G != 16) return OM_NOALLOC_BAD_ARGS;
+  const size_t np = (size_t)(max_ctx + om::ATT_PART - 1) / om::ATT_PART;
+  const size_t need = (size_t)rows * Hq * np * (head_dim + 2);
+  if (need > OM_NOALLOC_SCRATCH_FLOATS) return OM_NOALLOC_TOO_LARGE;
+  float* scratch = om_noalloc_scratch_ptr();
+  if (!scratch) return OM_NOALLOC_CUDA_ERROR;
+  om::AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_ld = q_ld;
+  a.kc = static_cast<const __nv_bfloat16*>(k_cache);
+  a.vc = static_cast<const __nv_bfloat16*>(v_cache);
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks;
+  a.row_seq = row_seq;
+  a.row_ctx = row_ctx;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_ld = out_ld;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.NP = (int)np;
+  a.part_o = scratch;
+  a.part_ml = scratch + (size_t)rows * Hq * np * head_dim;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.num_blocks = num_blocks;
+  a.status = status;
+  try {
+    if (head_dim == 128)
+      om::launch_d<128>(a, rows, G, stream);
+    else
+      om::launch_d<64>(a, rows, G, stream);
+  } catch (...) {
+    return OM_NOALLOC_CUDA_ERROR;
+  }
+  return OM_NOALLOC_OK;
+}
