@@ -19,15 +19,21 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int ld, const in
                                const int* __restrict__ slots, __nv_bfloat16* __restrict__ kc,
                                __nv_bfloat16* __restrict__ vc, const float* __restrict__ inv_freq, int Hq, int Hkv,
                                int D, int mode, int num_slots, int* status) {
+  __shared__ float cs[2][128];
   const int t = blockIdx.x;
   const int pos = positions[t];
   const int half = D / 2;
   __nv_bfloat16* row = qkv + (size_t)t * ld;
   const int rot_heads = Hq + Hkv;
-  for (int i = threadIdx.x; i < rot_heads * half; i += blockDim.x) {
-    const int h = i / half, j = i % half;
-    float s, c;
-    sincosf((float)pos * inv_freq[j], &s, &c);
+  // angles once per token, shared by all heads of this CTA
+  for (int j = threadIdx.x; j < half; j += blockDim.x) sincosf((float)pos * inv_freq[j], &cs[0][j], &cs[1][j]);
+  __syncthreads();
+  // blockIdx.y splits the heads across CTAs
+  const int hpb = (rot_heads + gridDim.y - 1) / gridDim.y;
+  const int h0 = blockIdx.y * hpb, h1 = min(rot_heads, h0 + hpb);
+  for (int i = threadIdx.x; i < (h1 - h0) * half; i += blockDim.x) {
+    const int h = h0 + i / half, j = i % half;
+    const float s = cs[0][j], c = cs[1][j];
     __nv_bfloat16* hp = row + h * D;
     const int i0 = mode == 0 ? 2 * j : j;
     const int i1 = mode == 0 ? 2 * j + 1 : j + half;
@@ -39,7 +45,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int ld, const in
   const int slot = slots[t];
   if (slot < 0) return;
   if (slot >= num_slots) {
-    if (threadIdx.x == 0) record_error(status, OM_ERR_BOUNDS);
+    if (threadIdx.x == 0 && blockIdx.y == 0) record_error(status, OM_ERR_BOUNDS);
     return;
   }
   const int blk = slot >> 4, off = slot & 15;
@@ -47,8 +53,11 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int ld, const in
   for (int i = threadIdx.x; i < Hkv * nv; i += blockDim.x) {
     const int h = i / nv, c = i % nv;
     const size_t dst = (((size_t)blk * Hkv + h) * 16 + off) * D;
-    reinterpret_cast<uint4*>(kc + dst)[c] = reinterpret_cast<const uint4*>(row + (Hq + h) * D)[c];
-    reinterpret_cast<uint4*>(vc + dst)[c] = reinterpret_cast<const uint4*>(row + (Hq + Hkv + h) * D)[c];
+    // K heads are written by the CTA that rotated them, V heads by CTA y = 0
+    if (Hq + h >= h0 && Hq + h < h1)
+      reinterpret_cast<uint4*>(kc + dst)[c] = reinterpret_cast<const uint4*>(row + (Hq + h) * D)[c];
+    if (blockIdx.y == 0)
+      reinterpret_cast<uint4*>(vc + dst)[c] = reinterpret_cast<const uint4*>(row + (Hq + Hkv + h) * D)[c];
   }
 }
 
@@ -84,7 +93,9 @@ void om_rope_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor slots,
   TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == D / 2, "rope_kv: inv_freq");
   const int T = positions.numel();
   if (T == 0) return;
-  om::rope_kv_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+  TORCH_CHECK(D / 2 <= 128, "rope_kv: head_dim <= 256");
+  const int ysplit = std::max<int64_t>(1, std::min<int64_t>(8, (Hq + Hkv) / 8));
+  om::rope_kv_kernel<<<dim3(T, ysplit), 128, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int>(),
       slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), inv_freq.data_ptr<float>(), Hq, Hkv, D, mode,

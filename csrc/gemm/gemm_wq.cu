@@ -74,10 +74,22 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qweight, torch::Tensor scales, in
     ws_bytes = workspace->numel() * sizeof(float);
   }
   if (ws && N % 4 == 0) {
-    if (force_splits > 0)
+    if (force_splits > 0) {
       splits = (int)force_splits;
-    else if (units < sms)
-      splits = std::max(1, sms / units);
+    } else {
+      // smallest split count whose work units fill the persistent grid's rounds
+      // to within 6% (each split keeps >= 8 K blocks)
+      double best = 1e30;
+      for (int s = 1; s <= 16 && g.num_kb / s >= 8; ++s) {
+        const int u = units * s;
+        const double rounds = (double)((u + sms - 1) / sms);
+        const double waste = rounds * sms / u;  // >= 1
+        if (waste < best * 0.94) {
+          best = waste;
+          splits = s;
+        }
+      }
+    }
     splits = std::min<int>(splits, g.num_kb);
     splits = std::min<int>(splits, (int)std::max<size_t>(1, ws_bytes / ((size_t)M * N * sizeof(float))));
   }

@@ -14,7 +14,7 @@
 //   warp 1       MMA issuer (one elected lane), 2 TMEM accumulators
 //   warp 2       TMEM allocation
 //   warps 4..7   epilogue (shared with the bf16 kernel)
-//   warps 8..15  dequant: thread t expands half a row (32 k) of the weight tile
+//   warps 8..15  dequant: each warp expands whole stages (128 rows x 64 k), round robin
 //
 // SWAP = true (decode): A = weight tile (M = 128 weight rows), B = activations
 // (N = BX tokens); the epilogue writes Y[token][row]. SWAP = false (prefill):
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(512, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&wready[s], 8);
+      mbar_init(&wready[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -193,44 +193,58 @@ __global__ void __launch_bounds__(512, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 256;
-    const int row = t >> 1, half = t & 1;
-    int it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-      int tr, tc, sp;
-      unit_coords(g, u, tr, tc, sp);
-      const int kb0 = sp * g.kb_per_split;
-      const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const int s = it % C::STAGES;
-        const uint32_t ph = (it / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
-        uint8_t* st = smem + s * C::STAGE_BYTES;
-        const uint8_t* raw = st + C::W_BYTES + C::X_BYTES;
-        uint8_t* wrow = st + row * 128;
-        const uint32_t sw = row & 7;
-        const int cbase = half * 4;
-        if (QT == WQ_Q4) {
-          const uint4 pk = *reinterpret_cast<const uint4*>(raw + row * 32 + half * 16);
-          const __nv_bfloat16 sc = reinterpret_cast<const __nv_bfloat16*>(raw + C::RAW_Q)[half * 128 + row];
-          __nv_bfloat162 b2 = __halves2bfloat162(sc, sc);
-          const uint32_t s2 = *reinterpret_cast<uint32_t*>(&b2);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 0) ^ sw) << 4)) = q4_chunk(pk.x, pk.y, 0, s2);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 1) ^ sw) << 4)) = q4_chunk(pk.z, pk.w, 0, s2);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 2) ^ sw) << 4)) = q4_chunk(pk.x, pk.y, 4, s2);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 3) ^ sw) << 4)) = q4_chunk(pk.z, pk.w, 4, s2);
-        } else {
-          const uint4 p0 = *reinterpret_cast<const uint4*>(raw + row * 64 + half * 32);
-          const uint4 p1 = *reinterpret_cast<const uint4*>(raw + row * 64 + half * 32 + 16);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 0) ^ sw) << 4)) = i8_chunk(p0.x, p0.y);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 1) ^ sw) << 4)) = i8_chunk(p0.z, p0.w);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 2) ^ sw) << 4)) = i8_chunk(p1.x, p1.y);
-          *reinterpret_cast<uint4*>(wrow + (((cbase + 3) ^ sw) << 4)) = i8_chunk(p1.z, p1.w);
+    // Warp d handles every NDQ-th stage iteration on its own (one fence per
+    // stage per warp), so up to NDQ stages are expanded concurrently. NDQ never
+    // exceeds the ring depth, so two warps never wait on the same barrier phase.
+    constexpr int NDQ = C::STAGES < 8 ? C::STAGES : 8;
+    const int d = warp - 8;
+    if (d < NDQ) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        int tr, tc, sp;
+        unit_coords(g, u, tr, tc, sp);
+        const int kb0 = sp * g.kb_per_split;
+        const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if (it % NDQ != d) continue;
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          const uint8_t* raw = st + C::W_BYTES + C::X_BYTES;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int row = lane + 32 * j;
+            uint8_t* wrow = st + row * 128;
+            const uint32_t sw = row & 7;
+            if (QT == WQ_Q4) {
+              const uint4 p0 = *reinterpret_cast<const uint4*>(raw + row * 32);
+              const uint4 p1 = *reinterpret_cast<const uint4*>(raw + row * 32 + 16);
+              const uint16_t* sc = reinterpret_cast<const uint16_t*>(raw + C::RAW_Q);
+              const uint32_t s0 = (uint32_t)sc[row] * 0x10001u;
+              const uint32_t s1 = (uint32_t)sc[128 + row] * 0x10001u;
+              *reinterpret_cast<uint4*>(wrow + ((0 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 0, s0);
+              *reinterpret_cast<uint4*>(wrow + ((1 ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 0, s0);
+              *reinterpret_cast<uint4*>(wrow + ((2 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 4, s0);
+              *reinterpret_cast<uint4*>(wrow + ((3 ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 4, s0);
+              *reinterpret_cast<uint4*>(wrow + ((4 ^ sw) << 4)) = q4_chunk(p1.x, p1.y, 0, s1);
+              *reinterpret_cast<uint4*>(wrow + ((5 ^ sw) << 4)) = q4_chunk(p1.z, p1.w, 0, s1);
+              *reinterpret_cast<uint4*>(wrow + ((6 ^ sw) << 4)) = q4_chunk(p1.x, p1.y, 4, s1);
+              *reinterpret_cast<uint4*>(wrow + ((7 ^ sw) << 4)) = q4_chunk(p1.z, p1.w, 4, s1);
+            } else {
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const uint4 p = *reinterpret_cast<const uint4*>(raw + row * 64 + h * 16);
+                *reinterpret_cast<uint4*>(wrow + (((2 * h) ^ sw) << 4)) = i8_chunk(p.x, p.y);
+                *reinterpret_cast<uint4*>(wrow + (((2 * h + 1) ^ sw) << 4)) = i8_chunk(p.z, p.w);
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wready[s]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&wready[s]);
       }
     }
   } else if (warp >= 4) {

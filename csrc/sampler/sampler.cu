@@ -1,14 +1,17 @@
-// Token sampler: temperature -> top-k -> top-p -> draw, one CTA per row.
+// Token sampler: temperature -> top-k -> top-p -> draw.
 //
 // The reference sampler (openmini-server/src/model/inference/sampler.rs:220-450,
 // openmini-server/src/model/inference/model.rs:3970) sorts the vocabulary. Here
-// the top-k and top-p cut-offs are found without sorting by an MSB-first radix
-// select over order-preserving 32-bit keys of the scaled logits (4 passes of
-// 8-bit histograms in shared memory): counts for top-k, probability mass for
-// top-p (the smallest prefix, in descending order, whose mass reaches p; ties
-// at the cut-off are kept). The draw is a Gumbel-max race among the kept tokens
-// with Philox-4x32-10 counter-based uniforms (Salmon et al., SC'11), so a
-// (seed, offset) pair reproduces the draw exactly.
+// each row is handled by one thread-block cluster of SCL CTAs: every CTA keeps
+// its slice of the row in registers, and the top-k / top-p cut-offs are found
+// without sorting by a bitwise binary search over order-preserving keys of the
+// logits (16-bit keys for bf16 logits, 32-bit for fp32): each probe is a plain
+// count (top-k) or probability-mass (top-p) reduction, combined across the
+// cluster through distributed shared memory. Top-p keeps the smallest
+// descending prefix whose mass reaches p (ties at the cut-off are kept), over
+// the top-k-restricted distribution. The draw is a Gumbel-max race among the
+// kept tokens with Philox-4x32-10 counter-based uniforms (Salmon et al.,
+// SC'11), so a (seed, offset) pair reproduces the draw exactly.
 //
 // Outputs: the token, its log-probability under the temperature-scaled full
 // distribution, and optionally the kept set as a bitmask (bit i of word i/32)
@@ -17,6 +20,9 @@
 #include "../common/om_ptx.cuh"
 
 namespace om {
+
+constexpr int SCL = 8;    // CTAs per row (portable cluster size)
+constexpr int SNT = 512;  // threads per CTA
 
 __device__ __forceinline__ uint32_t f2key(float f) {
   uint32_t b = __float_as_uint(f);
@@ -46,7 +52,7 @@ __device__ __forceinline__ float ld_logit<__nv_bfloat16>(const __nv_bfloat16* p,
 
 struct SampleArgs {
   const void* logits;
-  int ld, V;
+  int ld, V, chunk;  // chunk: elements per CTA (multiple of 32)
   const float* temperature;
   const float* top_p;
   const int* top_k;
@@ -56,150 +62,181 @@ struct SampleArgs {
   uint32_t* keep_mask;  // [B, ceil(V/32)] or null
 };
 
-constexpr int SNT = 1024;
-
-template <int NT>
-__device__ __forceinline__ float bsum(float v, float* sh) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < NT / 32 ? sh[threadIdx.x] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) sh[32] = t;
-  }
-  __syncthreads();
-  return sh[32];
+// ---------------------------------------------------------------- cluster helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_dsmem_u64(uint32_t addr) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+  return v;
 }
 
-// Radix select over keys of x = logit/T - max. mode 0: largest cutoff with
-// count(key >= cutoff) >= target. mode 1: largest cutoff with
-// mass(key >= cutoff) >= target, restricted to keys >= floor_key.
-template <typename T>
-__device__ uint32_t radix_cutoff(const T* row, int V, float inv_t, float mx, int mode, float target,
-                                 uint32_t floor_key, float* hist /*256*/, float* sh) {
-  uint32_t prefix = 0, pmask = 0;
-  float above = 0.f;  // count / mass of elements strictly above the chosen prefix
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += SNT) hist[i] = 0.f;
-    __syncthreads();
-    for (int i = threadIdx.x; i < V; i += SNT) {
-      const float x = ld_logit<T>(row, i) * inv_t - mx;
-      const uint32_t k = f2key(x);
-      if (k < floor_key) continue;
-      if ((k & pmask) != prefix) continue;
-      const float w = mode == 0 ? 1.f : __expf(x);
-      atomicAdd(&hist[(k >> shift) & 255u], w);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float acc = above;
-      int d = 255;
-      for (; d > 0; --d) {
-        if (acc + hist[d] >= target) break;
-        acc += hist[d];
-      }
-      sh[40] = acc;
-      sh[41] = __int_as_float(d);
-    }
-    __syncthreads();
-    above = sh[40];
-    const uint32_t d = (uint32_t)__float_as_int(sh[41]);
-    prefix |= d << shift;
-    pmask |= 255u << shift;
-    __syncthreads();
+struct SampleSmem {
+  float warp_part[SNT / 32];
+  float slot[2];                 // this CTA's partial, double-buffered by pass parity
+  unsigned long long best_warp[SNT / 32];
+  unsigned long long best;
+};
+
+// Sum of v over the cluster (op 0) or max (op 1); every thread gets the result.
+__device__ __forceinline__ float cluster_reduce(float v, int op, SampleSmem& sm, int& pass) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = op ? fmaxf(v, w) : v + w;
   }
-  return prefix;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sm.warp_part[warp] = v;
+  __syncthreads();
+  const int buf = pass & 1;
+  if (warp == 0) {
+    float t = lane < SNT / 32 ? sm.warp_part[lane] : (op ? -INFINITY : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, t, o);
+      t = op ? fmaxf(t, w) : t + w;
+    }
+    if (lane == 0) sm.slot[buf] = t;
+  }
+  cluster_sync();
+  const uint32_t a = smem_u32(&sm.slot[buf]);
+  float r = op ? -INFINITY : 0.f;
+#pragma unroll
+  for (int c = 0; c < SCL; ++c) {
+    const float w = ld_dsmem_f32(mapa(a, c));
+    r = op ? fmaxf(r, w) : r + w;
+  }
+  ++pass;
+  return r;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(SNT) sample_kernel(const SampleArgs a) {
-  __shared__ float sh[48];
-  __shared__ float hist[256];
-  __shared__ unsigned long long best;
-  const int b = blockIdx.x;
+template <typename T, int EPT>
+__global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel(const SampleArgs a) {
+  __shared__ SampleSmem sm;
+  const int b = blockIdx.x / SCL;
+  const uint32_t crank = cluster_rank();
   const T* row = reinterpret_cast<const T*>(a.logits) + (size_t)b * a.ld;
   const int V = a.V;
+  const int base = (int)crank * a.chunk;
   const float temp = a.temperature[b];
   const bool greedy = !(temp > 0.f);
   const float inv_t = greedy ? 1.f : 1.f / temp;
+  constexpr int KEY_SHIFT = std::is_same<T, float>::value ? 0 : 16;
+  constexpr int KEY_BITS = 32 - KEY_SHIFT;
+  int pass = 0;
 
-  // max of scaled logits
-  float mx = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += SNT) mx = fmaxf(mx, ld_logit<T>(row, i) * inv_t);
+  float x[EPT];
+  uint32_t key[EPT];
+  float lmax = -INFINITY;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = mx;
-  if (threadIdx.x == 0) best = 0ull;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = sh[threadIdx.x];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
-    if (threadIdx.x == 0) sh[34] = t;
+  for (int e = 0; e < EPT; ++e) {
+    const int i = base + e * SNT + (int)threadIdx.x;
+    const bool in = (e * SNT + (int)threadIdx.x) < a.chunk && i < V;
+    const float l = in ? ld_logit<T>(row, i) : -INFINITY;
+    x[e] = l * inv_t;
+    key[e] = in ? (f2key(l) >> KEY_SHIFT) : 0u;  // key 0: never kept
+    lmax = fmaxf(lmax, x[e]);
   }
-  __syncthreads();
-  mx = sh[34];
-  __syncthreads();
-
+  const float mx = cluster_reduce(lmax, 1, sm, pass);
   float z = 0.f;
-  for (int i = threadIdx.x; i < V; i += SNT) z += __expf(ld_logit<T>(row, i) * inv_t - mx);
-  z = bsum<SNT>(z, sh);
-  const float logz = logf(z);
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) z += __expf(x[e] - mx);
+  z = cluster_reduce(z, 0, sm, pass);
 
-  uint32_t cut = 0;  // keep keys >= cut
+  uint32_t cut = 1;  // keep key >= cut (real keys are >= 1)
   if (greedy) {
-    cut = f2key(0.f);  // only the max survives (ties -> lowest index below)
+    // keep only the maximum (ties broken toward the lowest index below)
+    cut = 0xFFFFFFFFu;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e)
+      if (x[e] == mx && key[e] != 0u) cut = min(cut, key[e]);
+    cut = (uint32_t)(-cluster_reduce(-(float)cut, 1, sm, pass));  // exact for 16-bit keys
+    if (KEY_BITS == 32) {
+      // fp32 keys may not survive the float round trip: fall back to comparing values
+      cut = 0;
+    }
   } else {
     const int k = a.top_k ? a.top_k[b] : 0;
-    if (k > 0 && k < V) cut = radix_cutoff<T>(row, V, inv_t, mx, 0, (float)k, 0u, hist, sh);
+    if (k > 0 && k < V) {
+      uint32_t t = 0;
+      for (int bit = KEY_BITS - 1; bit >= 0; --bit) {
+        const uint32_t cand = t | (1u << bit);
+        float c = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) c += key[e] >= cand ? 1.f : 0.f;
+        if (cluster_reduce(c, 0, sm, pass) >= (float)k) t = cand;
+      }
+      cut = max(cut, t);
+    }
     const float p = a.top_p ? a.top_p[b] : 1.f;
     if (p < 1.f) {
       float zk = z;
-      if (cut != 0) {
+      if (cut > 1) {
         float s = 0.f;
-        for (int i = threadIdx.x; i < V; i += SNT) {
-          const float x = ld_logit<T>(row, i) * inv_t - mx;
-          if (f2key(x) >= cut) s += __expf(x);
-        }
-        zk = bsum<SNT>(s, sh);
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) s += key[e] >= cut ? __expf(x[e] - mx) : 0.f;
+        zk = cluster_reduce(s, 0, sm, pass);
       }
-      const uint32_t cp = radix_cutoff<T>(row, V, inv_t, mx, 1, p * zk, cut, hist, sh);
-      cut = max(cut, cp);
+      const float target = p * zk;
+      uint32_t t = 0;
+      for (int bit = KEY_BITS - 1; bit >= 0; --bit) {
+        const uint32_t cand = t | (1u << bit);
+        if (cand < cut) {  // below the top-k floor every probe passes
+          t = cand;
+          continue;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) s += key[e] >= cand ? __expf(x[e] - mx) : 0.f;
+        if (cluster_reduce(s, 0, sm, pass) >= target) t = cand;
+      }
+      cut = max(cut, t);
     }
   }
 
-  // Gumbel-max draw among kept tokens; pack (score key, ~index) to take the
-  // max score and, on ties, the lowest index.
+  // Gumbel-max draw among kept tokens; pack (score key, ~index) so the max
+  // picks the highest score and, on ties, the lowest index.
   const uint32_t seed_lo = (uint32_t)a.rng[2 * b], seed_hi = (uint32_t)((uint64_t)a.rng[2 * b] >> 32);
   const uint64_t off = (uint64_t)a.rng[2 * b + 1];
   unsigned long long mine = 0ull;
   const int nwords = (V + 31) / 32;
-  for (int base = 0; base < V; base += SNT) {
-    const int i = base + threadIdx.x;
-    bool keep = false;
-    if (i < V) {
-      const float x = ld_logit<T>(row, i) * inv_t - mx;
-      keep = f2key(x) >= cut;
-      if (keep) {
-        float score = x;
-        if (!greedy) {
-          uint32_t c[4] = {(uint32_t)i, (uint32_t)b, (uint32_t)off, (uint32_t)(off >> 32)};
-          philox4x32_10(c, seed_lo, seed_hi);
-          const float u = ((float)c[0] + 0.5f) * 2.3283064365386963e-10f;
-          score = x - logf(-logf(u));
-        }
-        const unsigned long long cand =
-            ((unsigned long long)f2key(score) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
-        if (cand > mine) mine = cand;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    const int li = e * SNT + (int)threadIdx.x;
+    const int i = base + li;
+    bool keep = key[e] != 0u && (greedy && KEY_BITS == 32 ? x[e] == mx : key[e] >= cut);
+    if (keep) {
+      float score = x[e] - mx;
+      if (!greedy) {
+        uint32_t c[4] = {(uint32_t)i, (uint32_t)b, (uint32_t)off, (uint32_t)(off >> 32)};
+        philox4x32_10(c, seed_lo, seed_hi);
+        const float u = ((float)c[0] + 0.5f) * 2.3283064365386963e-10f;
+        score -= logf(-logf(u));
       }
+      const unsigned long long cand =
+          ((unsigned long long)f2key(score) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+      if (cand > mine) mine = cand;
     }
     const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (a.keep_mask && (threadIdx.x & 31) == 0) {
-      const int w = (base + (threadIdx.x & ~31)) / 32;
+    if (a.keep_mask && lane == 0 && li - lane < a.chunk) {
+      const int w = (base + li - lane) / 32;
       if (w < nwords) a.keep_mask[(size_t)b * nwords + w] = bal;
     }
   }
@@ -208,13 +245,26 @@ __global__ void __launch_bounds__(SNT) sample_kernel(const SampleArgs a) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, mine, o);
     if (other > mine) mine = other;
   }
-  if ((threadIdx.x & 31) == 0) atomicMax(&best, mine);
+  if (lane == 0) sm.best_warp[warp] = mine;
   __syncthreads();
   if (threadIdx.x == 0) {
-    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
-    a.out_tok[b] = tok;
-    if (a.out_logprob) a.out_logprob[b] = ld_logit<T>(row, tok) * inv_t - mx - logz;
+    unsigned long long m = 0ull;
+    for (int w = 0; w < SNT / 32; ++w) m = sm.best_warp[w] > m ? sm.best_warp[w] : m;
+    sm.best = m;
   }
+  cluster_sync();
+  if (crank == 0 && threadIdx.x == 0) {
+    unsigned long long m = 0ull;
+    const uint32_t addr = smem_u32(&sm.best);
+    for (int c = 0; c < SCL; ++c) {
+      const unsigned long long w = ld_dsmem_u64(mapa(addr, c));
+      m = w > m ? w : m;
+    }
+    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
+    a.out_tok[b] = tok;
+    if (a.out_logprob) a.out_logprob[b] = ld_logit<T>(row, tok) * inv_t - mx - logf(z);
+  }
+  cluster_sync();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
 // logit -> logit / penalty if > 0 else logit * penalty, for each distinct id in
@@ -238,6 +288,21 @@ __global__ void rep_penalty_kernel(T* logits, int ld, int V, const int* prev, in
   }
 }
 
+template <typename T>
+static void launch_sample(const SampleArgs& a, int B, cudaStream_t st) {
+  const int ept = (a.chunk + SNT - 1) / SNT;
+  if (ept <= 8)
+    sample_kernel<T, 8><<<B * SCL, SNT, 0, st>>>(a);
+  else if (ept <= 16)
+    sample_kernel<T, 16><<<B * SCL, SNT, 0, st>>>(a);
+  else if (ept <= 32)
+    sample_kernel<T, 32><<<B * SCL, SNT, 0, st>>>(a);
+  else if (ept <= 48)
+    sample_kernel<T, 48><<<B * SCL, SNT, 0, st>>>(a);
+  else
+    TORCH_CHECK(false, "sample: vocabulary too large (max ", SCL * SNT * 48, ")");
+}
+
 }  // namespace om
 
 void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
@@ -254,6 +319,7 @@ void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor to
   a.logits = logits.data_ptr();
   a.ld = logits.stride(0);
   a.V = V;
+  a.chunk = ((V + om::SCL - 1) / om::SCL + 31) / 32 * 32;
   a.temperature = temperature.data_ptr<float>();
   a.top_p = top_p.data_ptr<float>();
   a.top_k = top_k.data_ptr<int>();
@@ -267,9 +333,9 @@ void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor to
   }
   auto st = at::cuda::getCurrentCUDAStream().stream();
   if (logits.scalar_type() == at::kFloat)
-    om::sample_kernel<float><<<B, om::SNT, 0, st>>>(a);
+    om::launch_sample<float>(a, B, st);
   else if (logits.scalar_type() == at::kBFloat16)
-    om::sample_kernel<__nv_bfloat16><<<B, om::SNT, 0, st>>>(a);
+    om::launch_sample<__nv_bfloat16>(a, B, st);
   else
     TORCH_CHECK(false, "sample: logits must be fp32 or bf16");
   OM_LAUNCH_CHECK();
