@@ -24,6 +24,9 @@ void om_kv_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::T
 void om_paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                         torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor out, torch::Tensor workspace,
                         int64_t Hq, int64_t max_ctx, double scale, torch::Tensor status);
+void om_paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                           torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor out, torch::Tensor workspace,
+                           int64_t Hq, int64_t max_ctx, double scale, torch::Tensor status);
 int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_t max_ctx);
 void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
                torch::Tensor rng, torch::Tensor out_tok, c10::optional<torch::Tensor> out_logprob,
@@ -59,6 +62,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv", &om_rope_kv);
   m.def("kv_write", &om_kv_write);
   m.def("paged_attention", &om_paged_attention);
+  m.def("paged_attention_tc", &om_paged_attention_tc, "tcgen05 paged decode attention (head_dim 128)");
   m.def("paged_attention_workspace", &om_paged_attention_workspace);
   m.def("sample", &om_sample, py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("top_k"),
         py::arg("rng"), py::arg("out_tok"), py::arg("out_logprob") = py::none(),

@@ -68,4 +68,22 @@ inline CUtensorMap make_tmap_2d(const void* ptr, CUtensorMapDataType dt, int ele
   return m;
 }
 
+// 3-D tensor [d2, d1, d0] (d0 innermost) with strides s1, s2 in elements.
+inline CUtensorMap make_tmap_3d(const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t d0, uint64_t d1,
+                                uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                                CUtensorMapSwizzle sw) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1 * (uint64_t)elem_bytes, s2 * (uint64_t)elem_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((strides[0] & 15) == 0 && (strides[1] & 15) == 0, "TMA strides must be multiples of 16 bytes");
+  CUresult r = encode_fn()(&m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3d) failed: ", (int)r);
+  return m;
+}
+
 }  // namespace om

@@ -65,7 +65,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 #pragma unroll
         for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
       } else {
-        for (int j = 0; j < ncol; ++j) dst[j] = f[j];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncol) dst[j] = f[j];
       }
     } else {
       float* dst = P + (size_t)sp * g.rows * g.cols;
@@ -96,10 +98,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
         *reinterpret_cast<uint4*>(dst + j) = o;
       }
     } else {
-      for (int j = 0; j < ncol; ++j) {
-        float t = f[j];
-        if (g.epi == EPI_RESID) t += __bfloat162float(rs[j]);
-        dst[j] = __float2bfloat16_rn(t);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < ncol) {
+          float t = f[j];
+          if (g.epi == EPI_RESID) t += __bfloat162float(rs[j]);
+          dst[j] = __float2bfloat16_rn(t);
+        }
       }
     }
   } else {

@@ -4,17 +4,30 @@
 //
 // The dequantisation is fused into the mainloop: the packed weight tile
 // (128 rows x 64 k) is brought into shared memory by TMA in its compact form,
-// eight dequant warps expand it into the bf16 operand tile in exactly the
+// dequant warps expand it into the bf16 operand tile in exactly the
 // 128-byte-swizzled K-major layout that tcgen05.mma reads, and the MMA issuer
 // consumes it. HBM therefore carries 0.56 (Q4) or 1 (I8) byte per weight
 // instead of 2.
 //
+// Three independent shared-memory rings keep the weight stream deep:
+//   raw ring  packed weight tiles (+ Q4 scales), up to 18 slots, filled by the
+//             weight producer, emptied by the dequant warp that expands them
+//   x ring    activation tiles (128-byte swizzle), filled by the activation
+//             producer, emptied by the MMA
+//   w ring    bf16 operand tiles, written by the dequant warps, emptied by the MMA
+// so an activation reload never waits behind a weight slot and ~50-70 KB of
+// packed weights stay in flight per SM.
+//
 // Roles (512 threads, one CTA per SM):
-//   warp 0       TMA producer: activation tile (swizzled) + packed weight tile + scales
+//   warp 0       TMA producer of the packed weights
+//   warp 3       TMA producer of the activations
 //   warp 1       MMA issuer (one elected lane), 2 TMEM accumulators
 //   warp 2       TMEM allocation
 //   warps 4..7   epilogue (shared with the bf16 kernel)
-//   warps 8..15  dequant: each warp expands whole stages (128 rows x 64 k), round robin
+//   warps 8..    dequant warps; warp d expands every NDQ-th K block and owns the
+//                raw and w slots congruent to d (mod NDQ), so each warp consumes
+//                its own slots strictly in order and never waits on a barrier
+//                two phases ahead of its producer.
 //
 // SWAP = true (decode): A = weight tile (M = 128 weight rows), B = activations
 // (N = BX tokens); the epilogue writes Y[token][row]. SWAP = false (prefill):
@@ -36,15 +49,24 @@ enum WQType : int { WQ_Q4 = 0, WQ_I8 = 1 };
 template <int BX, int QT>
 struct WqCfg {
   static constexpr int BK = 64;
-  static constexpr int W_BYTES = 128 * BK * 2;   // bf16 operand tile
-  static constexpr int X_BYTES = BX * BK * 2;
+  static constexpr int W_BYTES = 128 * BK * 2;  // bf16 operand tile
+  static constexpr int X_BYTES = BX * BK * 2;   // activation tile
   static constexpr int RAW_Q = QT == WQ_Q4 ? 128 * 32 : 128 * 64;
   static constexpr int RAW_S = QT == WQ_Q4 ? 2 * 128 * 2 : 0;
-  static constexpr int RAW_BYTES = RAW_Q + RAW_S;
-  static constexpr int STAGE_BYTES = ((W_BYTES + X_BYTES + RAW_BYTES + 1023) / 1024) * 1024;
-  static constexpr int STAGES_ = (200 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_ > 8 ? 8 : STAGES_;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
+  static constexpr int RAW_BYTES = RAW_Q + RAW_S;  // multiple of 16
+  static constexpr int NDQ = BX <= 64 ? 5 : (BX == 128 ? 4 : 3);  // dequant warps = w-ring depth
+  static constexpr int WD = NDQ;
+  static constexpr int X_BUDGET = BX <= 128 ? 64 * 1024 : 96 * 1024;
+  static constexpr int XD_ = X_BUDGET / X_BYTES;
+  static constexpr int XD = XD_ > 16 ? 16 : (XD_ < 2 ? 2 : XD_);
+  static constexpr int RAW_AVAIL = 200 * 1024 - WD * W_BYTES - XD * X_BYTES;
+  static constexpr int RD_ = RAW_AVAIL / RAW_BYTES > 18 ? 18 : RAW_AVAIL / RAW_BYTES;
+  static constexpr int RD = (RD_ / NDQ) * NDQ;  // multiple of NDQ (private slots per warp)
+  static_assert(RD >= NDQ, "raw ring must hold one slot per dequant warp");
+  static constexpr int X_OFF = WD * W_BYTES;
+  static constexpr int RAW_OFF = X_OFF + XD * X_BYTES;
+  static constexpr int BAR_OFF = ((RAW_OFF + RD * RAW_BYTES + 15) / 16) * 16;
+  static constexpr int SMEM_BYTES = BAR_OFF + (2 * WD + 2 * XD + 2 * RD + 4) * 8 + 16 + 1024;
 };
 
 __device__ __forceinline__ uint32_t q4_pair(uint32_t t, int shift, uint32_t s2) {
@@ -79,6 +101,7 @@ __device__ __forceinline__ uint4 i8_chunk(uint32_t w0, uint32_t w1) {
   return o;
 }
 
+
 template <int BX, int QT, bool SWAP>
 __global__ void __launch_bounds__(512, 1)
     gemm_wq_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
@@ -86,12 +109,19 @@ __global__ void __launch_bounds__(512, 1)
   using C = WqCfg<BX, QT>;
   constexpr int BN_MMA = SWAP ? BX : 128;
   constexpr int TMEM_COLS = 2 * BN_MMA < 32 ? 32 : 2 * BN_MMA;
+  constexpr int WD = C::WD, XD = C::XD, RD = C::RD, NDQ = C::NDQ;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
-  uint64_t* wready = full + C::STAGES;
-  uint64_t* empty = wready + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;
+  uint8_t* wbuf = smem;
+  uint8_t* xbuf = smem + C::X_OFF;
+  uint8_t* rawbuf = smem + C::RAW_OFF;
+  uint64_t* w_ready = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* w_empty = w_ready + WD;
+  uint64_t* x_full = w_empty + WD;
+  uint64_t* x_empty = x_full + XD;
+  uint64_t* raw_full = x_empty + XD;
+  uint64_t* raw_empty = raw_full + RD;
+  uint64_t* tfull = raw_empty + RD;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
@@ -100,10 +130,17 @@ __global__ void __launch_bounds__(512, 1)
   const int total_units = g.tiles_r * g.tiles_c * g.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&wready[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < WD; ++s) {
+      mbar_init(&w_ready[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    for (int s = 0; s < XD; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
+    }
+    for (int s = 0; s < RD; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -121,9 +158,13 @@ __global__ void __launch_bounds__(512, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 3) {
+    // ------------------------------------------------------------ producers
     if (elect_one()) {
+      const bool wq = warp == 0;
+      const int depth = wq ? RD : XD;
+      uint64_t* fullb = wq ? raw_full : x_full;
+      uint64_t* emptyb = wq ? raw_empty : x_empty;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
@@ -134,25 +175,26 @@ __global__ void __launch_bounds__(512, 1)
         const int kb0 = sp * g.kb_per_split;
         const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          uint8_t* xs = st + C::W_BYTES;
-          uint8_t* raw = xs + C::X_BYTES;
-          mbar_arrive_expect_tx(&full[s], C::X_BYTES + C::RAW_BYTES);
-          tma_load_2d(xs, &tmX, &full[s], kb * 64, xt * BX);
-          if (QT == WQ_Q4) {
-            tma_load_2d(raw, &tmQ, &full[s], kb * 32, wt * 128);
-            tma_load_2d(raw + C::RAW_Q, &tmS, &full[s], wt * 128, kb * 2);
+          const int s = it % depth;
+          const uint32_t ph = (it / depth) & 1;
+          if (!mbar_wait(&emptyb[s], ph ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
+          if (wq) {
+            uint8_t* raw = rawbuf + s * C::RAW_BYTES;
+            mbar_arrive_expect_tx(&fullb[s], C::RAW_BYTES);
+            if (QT == WQ_Q4) {
+              tma_load_2d(raw, &tmQ, &fullb[s], kb * 32, wt * 128);
+              tma_load_2d(raw + C::RAW_Q, &tmS, &fullb[s], wt * 128, kb * 2);
+            } else {
+              tma_load_2d(raw, &tmQ, &fullb[s], kb * 64, wt * 128);
+            }
           } else {
-            tma_load_2d(raw, &tmQ, &full[s], kb * 64, wt * 128);
+            mbar_arrive_expect_tx(&fullb[s], C::X_BYTES);
+            tma_load_2d(xbuf + s * C::X_BYTES, &tmX, &fullb[s], kb * 64, xt * BX);
           }
         }
       }
       if (!ok) {
-        for (int j = max(0, it - C::STAGES); j < it; ++j)
-          mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, nullptr, 0);
+        for (int j = max(0, it - depth); j < it; ++j) mbar_wait(&fullb[j % depth], (j / depth) & 1, nullptr, 0);
       }
     }
   } else if (warp == 1) {
@@ -172,13 +214,12 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN_MMA;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
-          if (!mbar_wait(&wready[s], ph, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
+          const int xs = it % XD, ws = it % WD;
+          if (!mbar_wait(&x_full[xs], (it / XD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
+          if (!mbar_wait(&w_ready[ws], (it / WD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t w_addr = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t x_addr = w_addr + C::W_BYTES;
+          const uint32_t w_addr = smem_u32(wbuf + ws * C::W_BYTES);
+          const uint32_t x_addr = smem_u32(xbuf + xs * C::X_BYTES);
           const uint32_t a_addr = SWAP ? w_addr : x_addr;
           const uint32_t b_addr = SWAP ? x_addr : w_addr;
 #pragma unroll
@@ -186,17 +227,14 @@ __global__ void __launch_bounds__(512, 1)
             tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32, 1024), smem_desc_sw128(b_addr + k * 32, 1024),
                        IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[s]);
+          tc_commit(&x_empty[xs]);
+          tc_commit(&w_empty[ws]);
         }
         if (ok) tc_commit(&tfull[acc]);
       }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
-    // Warp d handles every NDQ-th stage iteration on its own (one fence per
-    // stage per warp), so up to NDQ stages are expanded concurrently. NDQ never
-    // exceeds the ring depth, so two warps never wait on the same barrier phase.
-    constexpr int NDQ = C::STAGES < 8 ? C::STAGES : 8;
     const int d = warp - 8;
     if (d < NDQ) {
       int it = 0;
@@ -208,11 +246,11 @@ __global__ void __launch_bounds__(512, 1)
         const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           if (it % NDQ != d) continue;
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          const uint8_t* raw = st + C::W_BYTES + C::X_BYTES;
+          const int r = it % RD, s = it % WD;
+          if (!mbar_wait(&raw_full[r], (it / RD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
+          if (!mbar_wait(&w_empty[s], ((it / WD) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
+          const uint8_t* raw = rawbuf + r * C::RAW_BYTES;
+          uint8_t* st = wbuf + s * C::W_BYTES;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int row = lane + 32 * j;
@@ -221,9 +259,9 @@ __global__ void __launch_bounds__(512, 1)
             if (QT == WQ_Q4) {
               const uint4 p0 = *reinterpret_cast<const uint4*>(raw + row * 32);
               const uint4 p1 = *reinterpret_cast<const uint4*>(raw + row * 32 + 16);
-              const uint16_t* sc = reinterpret_cast<const uint16_t*>(raw + C::RAW_Q);
-              const uint32_t s0 = (uint32_t)sc[row] * 0x10001u;
-              const uint32_t s1 = (uint32_t)sc[128 + row] * 0x10001u;
+              const uint16_t* scp = reinterpret_cast<const uint16_t*>(raw + C::RAW_Q);
+              const uint32_t s0 = (uint32_t)scp[row] * 0x10001u;
+              const uint32_t s1 = (uint32_t)scp[128 + row] * 0x10001u;
               *reinterpret_cast<uint4*>(wrow + ((0 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 0, s0);
               *reinterpret_cast<uint4*>(wrow + ((1 ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 0, s0);
               *reinterpret_cast<uint4*>(wrow + ((2 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 4, s0);
@@ -243,7 +281,11 @@ __global__ void __launch_bounds__(512, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&wready[s]);
+          // the raw slot is released only after the whole tile has been read
+          if (lane == 0) {
+            mbar_arrive(&w_ready[s]);
+            mbar_arrive(&raw_empty[r]);
+          }
         }
       }
     }

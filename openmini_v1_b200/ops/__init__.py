@@ -170,8 +170,11 @@ def kv_write(k, v, slots, k_cache, v_cache):
     _native.C().kv_write(k, v, slots, k_cache, v_cache)
 
 
-def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, scale, max_ctx, out=None):
-    """Attention of query rows over the paged cache. ``max_ctx`` bounds the split count."""
+def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, scale, max_ctx, out=None, impl=None):
+    """Attention of query rows over the paged cache. ``max_ctx`` bounds the split count.
+
+    On the GPU, head_dim 128 with <= 16 query heads per KV head runs the
+    tensor-core kernel ("tc"); other shapes run the CUDA-core kernel ("simt")."""
     rows = row_seq.shape[0]
     D = k_cache.shape[3]
     if not q.is_cuda:
@@ -185,8 +188,11 @@ def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, sca
     c = ctx(q.device)
     need = _native.C().paged_attention_workspace(rows, Hq, D, max_ctx)
     ws = c.workspace("attn", need)
-    _native.C().paged_attention(q.reshape(rows, -1), k_cache, v_cache, block_tables, row_seq, row_ctx,
-                                out.view(rows, -1), ws, Hq, int(max_ctx), float(scale), c.status)
+    if impl is None:
+        impl = "tc" if D == 128 and Hq // k_cache.shape[1] <= 16 else "simt"
+    fn = _native.C().paged_attention_tc if impl == "tc" else _native.C().paged_attention
+    fn(q.reshape(rows, -1), k_cache, v_cache, block_tables, row_seq, row_ctx, out.view(rows, -1), ws, Hq,
+       int(max_ctx), float(scale), c.status)
     return out
 
 

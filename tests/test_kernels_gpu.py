@@ -139,8 +139,12 @@ def _paged_setup(S, Hkv, D, lens, nb, seed=0):
     return kc, vc, bt.to(DEV)
 
 
-@pytest.mark.parametrize("Hq,Hkv,D", [(8, 1, 128), (4, 2, 64), (32, 32, 128), (40, 8, 128), (64, 8, 128)])
-def test_paged_attention_decode(Hq, Hkv, D):
+@pytest.mark.parametrize("impl", ["tc", "simt"])
+@pytest.mark.parametrize("Hq,Hkv,D", [(8, 1, 128), (4, 2, 64), (32, 32, 128), (40, 8, 128), (64, 8, 128),
+                                      (16, 1, 128)])
+def test_paged_attention_decode(Hq, Hkv, D, impl):
+    if impl == "tc" and D != 128:
+        pytest.skip("tensor-core kernel needs head_dim 128")
     lens = [1, 17, 300, 513, 1500, 2049] if Hq <= 40 else [1, 17, 300, 2049]
     S = len(lens)
     kc, vc, bt = _paged_setup(S, Hkv, D, lens, 400, seed=20)
@@ -148,20 +152,21 @@ def test_paged_attention_decode(Hq, Hkv, D):
     rseq = torch.arange(S, dtype=torch.int32, device=DEV)
     rctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
     scale = 1 / math.sqrt(D)
-    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, scale, max_ctx=4096)
+    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, scale, max_ctx=4096, impl=impl)
     torch.cuda.synchronize()
     ops.check_status()
     _close(o.view(S, Hq, D), ref.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, scale))
 
 
-def test_paged_attention_prefill_rows():
+@pytest.mark.parametrize("impl", ["tc", "simt"])
+def test_paged_attention_prefill_rows(impl):
     Hq, Hkv, D = 8, 2, 128
     L = 700
     kc, vc, bt = _paged_setup(1, Hkv, D, [L], 64, seed=30)
     q = _rand(L, Hq, D, seed=31)
     rseq = torch.zeros(L, dtype=torch.int32, device=DEV)
     rctx = torch.arange(1, L + 1, dtype=torch.int32, device=DEV)
-    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, 0.088, max_ctx=L)
+    o = ops.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, 0.088, max_ctx=L, impl=impl)
     torch.cuda.synchronize()
     _close(o.view(L, Hq, D), ref.paged_attention(q, kc, vc, bt, rseq, rctx, Hq, 0.088))
 
