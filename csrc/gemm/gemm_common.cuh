@@ -21,6 +21,7 @@ struct GemmArgs {
   void* out;         // bf16 Y (EPI_STORE/EPI_RESID) or fp32 partials [splits][Ym][Yn]
   const __nv_bfloat16* resid;  // EPI_RESID: Y += resid (may alias out)
   const float* wscale;         // optional per-weight-row scale (INT8 weights)
+  const uint8_t* wtiles;       // quantised weights, pre-tiled (weight-only GEMM)
   int ldo;           // leading dimension of Y / resid (elements)
   int* status;
 };

@@ -3,7 +3,10 @@
 //   Y = X @ dequant(Wq)^T,  X bf16 [M, K],  Wq 4-bit block-32 (Q4) or INT8 per-row (I8)
 //
 // The dequantisation is fused into the mainloop: the packed weight tile
-// (128 rows x 64 k) is brought into shared memory by TMA in its compact form,
+// (128 rows x 64 k) is brought into shared memory in its compact form by one
+// bulk copy (the device weight format stores every tile contiguously:
+// [N/128][K/64][tile], tile = 128 rows x 32 B nibbles + 2 x 128 bf16 scales for
+// Q4, 128 rows x 64 B for INT8, so the weight stream is strictly sequential),
 // dequant warps expand it into the bf16 operand tile in exactly the
 // 128-byte-swizzled K-major layout that tcgen05.mma reads, and the MMA issuer
 // consumes it. HBM therefore carries 0.56 (Q4) or 1 (I8) byte per weight
@@ -104,8 +107,7 @@ __device__ __forceinline__ uint4 i8_chunk(uint32_t w0, uint32_t w1) {
 
 template <int BX, int QT, bool SWAP>
 __global__ void __launch_bounds__(512, 1)
-    gemm_wq_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
-                      const __grid_constant__ CUtensorMap tmS, const GemmArgs g) {
+    gemm_wq_tc_kernel(const __grid_constant__ CUtensorMap tmX, const GemmArgs g) {
   using C = WqCfg<BX, QT>;
   constexpr int BN_MMA = SWAP ? BX : 128;
   constexpr int TMEM_COLS = 2 * BN_MMA < 32 ? 32 : 2 * BN_MMA;
@@ -150,8 +152,6 @@ __global__ void __launch_bounds__(512, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmQ);
-    if (QT == WQ_Q4) tma_prefetch_desc(&tmS);
   }
   if (warp == 2) tmem_alloc(tmem_slot, TMEM_COLS);
   __syncthreads();
@@ -181,12 +181,8 @@ __global__ void __launch_bounds__(512, 1)
           if (wq) {
             uint8_t* raw = rawbuf + s * C::RAW_BYTES;
             mbar_arrive_expect_tx(&fullb[s], C::RAW_BYTES);
-            if (QT == WQ_Q4) {
-              tma_load_2d(raw, &tmQ, &fullb[s], kb * 32, wt * 128);
-              tma_load_2d(raw + C::RAW_Q, &tmS, &fullb[s], wt * 128, kb * 2);
-            } else {
-              tma_load_2d(raw, &tmQ, &fullb[s], kb * 64, wt * 128);
-            }
+            // one contiguous bulk copy per pre-tiled weight block (sequential DRAM stream)
+            bulk_load(raw, g.wtiles + ((size_t)wt * g.num_kb + kb) * C::RAW_BYTES, C::RAW_BYTES, &fullb[s]);
           } else {
             mbar_arrive_expect_tx(&fullb[s], C::X_BYTES);
             tma_load_2d(xbuf + s * C::X_BYTES, &tmX, &fullb[s], kb * 64, xt * BX);

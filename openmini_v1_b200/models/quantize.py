@@ -1,11 +1,13 @@
 """Weight-only quantised linear weights (4-bit block-32 and INT8 per output channel).
 
-``Q4Weight``: GGUF Q4_0 semantics (value = (q - 8) * d per 32-block). Device
-layout: qweight uint8 [N, K/2] in the ggml nibble order (byte i of a block =
-element i low nibble, element i + 16 high nibble) and scales bf16 transposed to
-[K/32, N] so a 128-row tile's scales are one contiguous TMA box.
-``Int8Weight``: q int8 [N, K], fp32 scale [N] (fp16-representable), applied in
-the GEMM epilogue.
+``Q4Weight``: GGUF Q4_0 semantics (value = (q - 8) * d per 32-block, ggml
+nibble order: byte i of a block = element i low nibble, element i + 16 high
+nibble). ``Int8Weight``: q int8 [N, K], fp32 scale [N] (fp16-representable),
+applied in the GEMM epilogue.
+
+Device format: the packed weight is stored pre-tiled, [ceil(N/128)][K/64][tile],
+each 128-row x 64-k tile contiguous (Q4 tiles also carry their bf16 block
+scales), so the GEMM streams weights with sequential bulk copies.
 
 ``linear`` runs the fused dequant tcgen05 GEMM on the GPU and the fp32 oracle
 on the CPU. Reference formats: openmini-server/src/model/inference/quant.rs:56-433
@@ -19,23 +21,64 @@ from .. import _native, ops
 from ..ops import reference as ref
 
 
+def _pad_rows(t: torch.Tensor, mult: int = 128) -> torch.Tensor:
+    n = t.shape[0]
+    pad = (-n) % mult
+    if pad == 0:
+        return t
+    return torch.cat([t, torch.zeros(pad, *t.shape[1:], dtype=t.dtype, device=t.device)])
+
+
+def tile_q4(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Row-major nibbles [N, K/2] + bf16 scales [N, K/32] -> tiles uint8 [ceil(N/128), K/64, 4608].
+
+    Tile (rt, kb) = 128 rows x 32 bytes of nibbles (K block kb) followed by the
+    2 x 128 bf16 scales of its two 32-blocks, scale index = block * 128 + row."""
+    N, K2 = q.shape
+    KB = K2 // 32
+    qp = _pad_rows(q).view(-1, 128, KB, 32).permute(0, 2, 1, 3).contiguous().view(-1, KB, 4096)
+    sp = _pad_rows(scales.view(torch.int16)).view(-1, 128, KB, 2).permute(0, 2, 3, 1).contiguous()
+    sp = sp.view(torch.uint8).view(-1, KB, 512)
+    return torch.cat([qp, sp], dim=2).contiguous()
+
+
+def untile_q4(tiles: torch.Tensor, N: int):
+    """Inverse of :func:`tile_q4`: (nibbles uint8 [N, K/2], bf16 scales [N, K/32])."""
+    NT, KB, _ = tiles.shape
+    q = tiles[:, :, :4096].reshape(NT, KB, 128, 32).permute(0, 2, 1, 3).reshape(NT * 128, KB * 32)[:N]
+    s = tiles[:, :, 4096:].contiguous().view(torch.int16).view(NT, KB, 2, 128).permute(0, 3, 1, 2)
+    s = s.reshape(NT * 128, KB * 2)[:N].contiguous().view(torch.bfloat16)
+    return q.contiguous(), s
+
+
+def tile_i8(q: torch.Tensor) -> torch.Tensor:
+    N, K = q.shape
+    KB = K // 64
+    return _pad_rows(q.view(torch.uint8)).view(-1, 128, KB, 64).permute(0, 2, 1, 3).contiguous().view(-1, KB, 8192)
+
+
+def untile_i8(tiles: torch.Tensor, N: int) -> torch.Tensor:
+    NT, KB, _ = tiles.shape
+    return tiles.view(NT, KB, 128, 64).permute(0, 2, 1, 3).reshape(NT * 128, KB * 64)[:N].contiguous().view(torch.int8)
+
+
 class Q4Weight:
+    """4-bit block-32 weight in the tiled device format (see :func:`tile_q4`)."""
     qtype = 0
 
-    def __init__(self, qweight: torch.Tensor, scales_t: torch.Tensor):
-        self.qweight = qweight          # uint8 [N, K/2]
-        self.scales_t = scales_t        # bf16 [K/32, N]
-        self.shape = (qweight.shape[0], qweight.shape[1] * 2)
+    def __init__(self, tiles: torch.Tensor, shape):
+        self.tiles = tiles
+        self.shape = tuple(shape)
 
     @property
     def device(self):
-        return self.qweight.device
+        return self.tiles.device
 
     @staticmethod
     def from_dense(w: torch.Tensor) -> "Q4Weight":
         N, K = w.shape
-        if K % 32:
-            raise ValueError("Q4 needs K % 32 == 0")
+        if K % 64:
+            raise ValueError("Q4 needs K % 64 == 0")
         w = w.to(torch.bfloat16).contiguous()
         if w.is_cuda:
             q = torch.empty(N, K // 2, dtype=torch.uint8, device=w.device)
@@ -43,19 +86,26 @@ class Q4Weight:
             _native.C().quantize_q4(w, q, s)
         else:
             q, s = ref.quantize_q4(w)
-        return Q4Weight(q, s.t().contiguous())
+        return Q4Weight(tile_q4(q, s), (N, K))
+
+    @staticmethod
+    def from_parts(q: torch.Tensor, scales_bf16: torch.Tensor) -> "Q4Weight":
+        return Q4Weight(tile_q4(q, scales_bf16), (q.shape[0], q.shape[1] * 2))
+
+    def parts(self):
+        return untile_q4(self.tiles, self.shape[0])
 
     def dequantize(self) -> torch.Tensor:
         N, K = self.shape
-        s = self.scales_t.t().contiguous()
-        if self.qweight.is_cuda:
+        q, s = self.parts()
+        if q.is_cuda:
             out = torch.empty(N, K, dtype=torch.bfloat16, device=self.device)
-            _native.C().dequant_q4(self.qweight, s, out)
+            _native.C().dequant_q4(q, s, out)
             return out
-        return ref.dequant_q4(self.qweight, s)
+        return ref.dequant_q4(q, s)
 
     def nbytes(self):
-        return self.qweight.numel() + self.scales_t.numel() * 2
+        return self.tiles.numel()
 
     def linear(self, x, out=None, resid=None):
         if not x.is_cuda:
@@ -64,42 +114,50 @@ class Q4Weight:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.qweight, self.scales_t, 0, self.shape[0], out, resid)
+        return _wq_linear(x, self.tiles, None, 0, self.shape[0], out, resid)
 
 
 class Int8Weight:
+    """INT8 per-output-channel weight: tiles uint8 [ceil(N/128), K/64, 8192] + fp32 scale [N]."""
     qtype = 1
 
-    def __init__(self, qweight: torch.Tensor, scale: torch.Tensor):
-        self.qweight = qweight          # int8 [N, K]
-        self.scale = scale              # fp32 [N]
-        self.shape = tuple(qweight.shape)
+    def __init__(self, tiles: torch.Tensor, scale: torch.Tensor, shape):
+        self.tiles = tiles
+        self.scale = scale
+        self.shape = tuple(shape)
 
     @property
     def device(self):
-        return self.qweight.device
+        return self.tiles.device
 
     @staticmethod
     def from_dense(w: torch.Tensor) -> "Int8Weight":
         w = w.to(torch.bfloat16).contiguous()
         N, K = w.shape
+        if K % 64:
+            raise ValueError("INT8 needs K % 64 == 0")
         if w.is_cuda:
             q = torch.empty(N, K, dtype=torch.int8, device=w.device)
             s = torch.empty(N, dtype=torch.float32, device=w.device)
             _native.C().quantize_int8(w, q, s)
         else:
             q, s = ref.quantize_int8(w)
-        return Int8Weight(q, s)
+        return Int8Weight(tile_i8(q), s, (N, K))
+
+    @property
+    def qweight(self):
+        return untile_i8(self.tiles, self.shape[0])
 
     def dequantize(self) -> torch.Tensor:
-        if self.qweight.is_cuda:
+        q = self.qweight
+        if q.is_cuda:
             out = torch.empty(self.shape, dtype=torch.bfloat16, device=self.device)
-            _native.C().dequant_int8(self.qweight, self.scale, out)
+            _native.C().dequant_int8(q, self.scale, out)
             return out
-        return ref.dequant_int8(self.qweight, self.scale)
+        return ref.dequant_int8(q, self.scale)
 
     def nbytes(self):
-        return self.qweight.numel() + self.scale.numel() * 4
+        return self.tiles.numel() + self.scale.numel() * 4
 
     def linear(self, x, out=None, resid=None):
         if not x.is_cuda:
@@ -111,10 +169,10 @@ class Int8Weight:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.qweight, self.scale, 1, self.shape[0], out, resid)
+        return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid)
 
 
-def _wq_linear(x, q, s, qtype, N, out, resid):
+def _wq_linear(x, tiles, scale, qtype, N, out, resid):
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
@@ -123,7 +181,7 @@ def _wq_linear(x, q, s, qtype, N, out, resid):
     c = ops.ctx(x.device)
     ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    _native.C().gemm_wq(x2, q, s, qtype, out.view(-1, N), r2, ws, c.status)
+    _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status)
     return out
 
 
