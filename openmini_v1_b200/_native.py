@@ -11,6 +11,8 @@ from __future__ import annotations
 
 import importlib
 
+import torch  # noqa: F401  (loads libc10 / libtorch that both extensions link against)
+
 _C = None
 _rt = None
 _C_err: Exception | None = None

@@ -126,3 +126,13 @@ def nbytes(typ: int, n: int) -> int:
     if n % per:
         raise ValueError(f"{GGMLType(typ).name}: {n} elements not a multiple of block {per}")
     return n // per * by
+
+
+def quantize_int8_rows(x: np.ndarray):
+    """Per-row symmetric INT8: (q int8 [N, K], fp16 scale [N]) with scale = absmax / 127."""
+    x = np.asarray(x, dtype=np.float32)
+    s = (np.abs(x).max(-1) / 127.0).astype(np.float16)
+    sf = s.astype(np.float32)
+    inv = np.where(sf > 0, 1.0 / np.where(sf > 0, sf, 1), 0)
+    q = np.clip(np.rint(x * inv[:, None]), -127, 127).astype(np.int8)
+    return q, s

@@ -30,7 +30,7 @@ def _params(body: dict, default_max: int = 16) -> SamplingParams:
     return SamplingParams(
         temperature=float(body.get("temperature", 1.0)), top_p=float(body.get("top_p", 1.0)),
         top_k=int(body.get("top_k", 0) or 0), repetition_penalty=float(body.get("repetition_penalty", 1.0)),
-        max_tokens=int(body.get("max_tokens", default_max) or default_max),
+        max_tokens=int(body["max_tokens"]) if body.get("max_tokens") is not None else default_max,
         min_tokens=int(body.get("min_tokens", 0)), stop_token_ids=list(body.get("stop_token_ids", []) or []),
         ignore_eos=bool(body.get("ignore_eos", False)), seed=body.get("seed"),
         logprobs=bool(body.get("logprobs", False)))

@@ -1,0 +1,114 @@
+"""Server entry point.
+
+    python -m openmini_v1_b200.serve.main [--config server.toml] [--preset tiny]
+        [--model path.gguf] [--http-port 8080] [--grpc-port 50051] [--gateway-port 0]
+
+Start-up mirrors openmini-server/src/main.rs:76-247 (logging, hardware report,
+config load + validation warnings, engine, servers, signal-driven shutdown),
+but the engine is the real one: a model from GGUF (or a random-init preset),
+the paged-KV continuous-batching engine, then HTTP (uvicorn), gRPC and the
+raw-TCP gateway on one event loop.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import logging
+import signal
+
+import torch
+
+from ..config.settings import load_config
+from ..engine.async_engine import AsyncLLMEngine
+from ..engine.engine import EngineConfig, LLMEngine
+from ..engine.tokenizer import ByteTokenizer, GGUFTokenizer
+from ..models.config import preset
+from ..models.llama import DecoderLM
+from ..utils.logging import init_logging
+from .gateway import Gateway
+from .grpc_server import OpenMiniServicer, SessionStore, start_grpc_server
+from .http import create_app
+from .metrics import Metrics
+
+log = logging.getLogger("openmini.server")
+
+
+def build_engine(cfg, preset_name=None, model_path=None, device=None):
+    device = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    fmt = cfg.model.weight_format if device != "cpu" else "bf16"
+    tokenizer = None
+    if model_path or (not preset_name and cfg.model.path and not cfg.model.preset):
+        from ..gguf.reader import GGUFReader
+        from ..models.loader import load_gguf_model
+        path = model_path or cfg.model.path
+        model = load_gguf_model(path, device=device, weight_format=fmt)
+        reader = GGUFReader(path)
+        if "tokenizer.ggml.tokens" in reader.metadata:
+            tokenizer = GGUFTokenizer.from_gguf(reader)
+    else:
+        mc = preset(preset_name or cfg.model.preset or "tiny")
+        if device == "cpu":
+            mc.dtype = "float32"
+        elif mc.dtype == "float32":
+            mc.dtype = "bfloat16"
+        model = DecoderLM(mc, device=device, weight_format=fmt)
+    tokenizer = tokenizer or ByteTokenizer(model.cfg.vocab_size)
+    e = cfg.engine
+    ecfg = EngineConfig(max_num_seqs=e.max_num_seqs, max_num_batched_tokens=e.max_num_batched_tokens,
+                        max_model_len=min(cfg.model.context_length, model.cfg.max_position),
+                        gpu_memory_utilization=e.gpu_memory_utilization, enable_prefix_cache=e.enable_prefix_cache,
+                        use_cuda_graph=e.use_cuda_graph and device != "cpu",
+                        eos_token_id=getattr(tokenizer, "eos_id", None))
+    return LLMEngine(model, ecfg), tokenizer
+
+
+async def serve(args):
+    cfg = load_config(args.config)
+    for w in cfg.validate():
+        log.warning("config: %s", w)
+    eng, tok = build_engine(cfg, args.preset, args.model)
+    aeng = AsyncLLMEngine(eng)
+    metrics = Metrics()
+    app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg)
+    import uvicorn
+    http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
+                                         log_level="warning"))
+    store = SessionStore(cfg.database.path if args.db else ":memory:")
+    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics),
+                                                 f"{cfg.server.host}:{args.grpc_port or cfg.server.port}",
+                                                 cfg.grpc.max_message_size_mb)
+    gw = Gateway(aeng, tok, cfg.server.max_connections)
+    gw_port = await gw.start(cfg.server.host, args.gateway_port) if args.gateway_port is not None else None
+    log.info("serving %s: http :%s grpc :%s gateway :%s", eng.model.cfg.name, http.config.port, gport, gw_port)
+    stop = asyncio.Event()
+    loop = asyncio.get_running_loop()
+    for sig in (signal.SIGINT, signal.SIGTERM):
+        try:
+            loop.add_signal_handler(sig, stop.set)
+        except NotImplementedError:
+            pass
+    http_task = asyncio.create_task(http.serve())
+    await stop.wait()
+    http.should_exit = True
+    await http_task
+    await grpc_server.stop(5)
+    await gw.stop()
+    aeng.shutdown()
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description="openmini_v1_b200 server")
+    p.add_argument("--config", default=None)
+    p.add_argument("--preset", default=None)
+    p.add_argument("--model", default=None)
+    p.add_argument("--http-port", type=int, default=None)
+    p.add_argument("--grpc-port", type=int, default=None)
+    p.add_argument("--gateway-port", type=int, default=None)
+    p.add_argument("--db", action="store_true", help="persist chat sessions to [database].path")
+    args = p.parse_args(argv)
+    init_logging()
+    asyncio.run(serve(args))
+
+
+if __name__ == "__main__":
+    main()
