@@ -132,11 +132,22 @@ class LLMEngine:
             for c in so.chunks:
                 self._sync_bm_tokens(c.req)
         fb, samp, rows_req = self._build(so)
+        want_routing = any(c.req.params.return_routing for c in so.chunks)
         if (so.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(so.chunks))
-                and not self._needs_eager_sampling(rows_req)):
+                and not self._needs_eager_sampling(rows_req) and not want_routing):
             tok, lp, mask = self.graphs.run(fb, samp, len(so.chunks))
         else:
+            if want_routing:
+                fb.record_routing = {}
             tok, lp, mask = self._forward_sample(fb, samp, rows_req)
+            if want_routing:
+                o = 0
+                for c in so.chunks:
+                    n = c.end - c.start
+                    if c.req.params.return_routing:
+                        for layer, ids in fb.record_routing.items():
+                            c.req.routing.setdefault(layer, []).append(ids[o:o + n].cpu())
+                    o += n
         return self._commit(so, rows_req, tok, lp, mask)
 
     def _sync_bm_tokens(self, r: Request):
@@ -203,7 +214,8 @@ class LLMEngine:
                 self.kv.v[i][dst].copy_(self.kv.v[i][src])
 
     def _needs_eager_sampling(self, rows_req):
-        return any(r.params.repetition_penalty != 1.0 or r.params.return_sampling_mask for r in rows_req)
+        return any(r.params.repetition_penalty != 1.0 or r.params.return_sampling_mask or r.params.return_routing
+                   for r in rows_req)
 
     def _build(self, so):
         """Stage metadata on pinned host memory and copy it to the device (one H2D per dtype)."""

@@ -27,6 +27,7 @@ class SamplingParams:
     seed: int | None = None
     logprobs: bool = False         # return the sampled token's log-prob
     return_sampling_mask: bool = False  # return the kept set of every step (RL replay)
+    return_routing: bool = False   # record MoE router choices for every processed token (Keep Routing)
 
     def validate(self):
         if self.temperature < 0:
@@ -63,6 +64,7 @@ class Request:
     output_token_ids: list = field(default_factory=list)
     output_logprobs: list = field(default_factory=list)
     sampling_masks: list = field(default_factory=list)
+    routing: dict = field(default_factory=dict)   # layer -> [int32 [n, k] per processed chunk]
     num_computed: int = 0          # tokens whose KV is in the cache
     first_token_time: float | None = None
     finish_time: float | None = None

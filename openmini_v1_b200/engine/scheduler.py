@@ -89,6 +89,7 @@ class Scheduler:
         self.running.remove(r)
         self.bm.free(r.seq_id)
         r.num_computed = 0
+        r.routing = {}  # recomputed from scratch on re-admission
         r.num_preemptions += 1
         r.status = RequestStatus.WAITING
         self.waiting.appendleft(r)
