@@ -40,6 +40,13 @@ void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out);
 void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale);
 void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
 
+void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor icache, torch::Tensor bt,
+                   torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor scores, torch::Tensor status);
+void om_dsa_topk(torch::Tensor scores, torch::Tensor row_ctx, int64_t k, torch::Tensor out_idx, torch::Tensor out_n);
+void om_dsa_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor bt,
+                      torch::Tensor row_seq, torch::Tensor sel, torch::Tensor sel_n, torch::Tensor out, int64_t Hq,
+                      double scale);
+
 #include "common/om_host.h"
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -74,4 +81,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequant_q4", &om_dequant_q4);
   m.def("quantize_int8", &om_quantize_int8);
   m.def("dequant_int8", &om_dequant_int8);
+  m.def("dsa_scores", &om_dsa_scores, "DSA indexer scores over the paged indexer-key cache");
+  m.def("dsa_topk", &om_dsa_topk, "per-row top-k key positions");
+  m.def("dsa_attention", &om_dsa_attention, "attention over selected keys of the paged cache");
 }

@@ -244,3 +244,36 @@ def test_repetition_penalty():
     a = ops.repetition_penalty(lg.clone(), prev, pen)
     b = ref.repetition_penalty(lg.clone().cpu(), prev.cpu(), pen.cpu())
     torch.testing.assert_close(a.cpu(), b)
+
+
+def test_dsa_kernels():
+    from openmini_v1_b200.models import dsa
+    rows, H, L = 5, 4, 1500
+    lens = [1500, 1024, 700, 1, 1300]
+    nb = 200
+    icache = _rand(nb, 16, 64, seed=70)
+    kc, vc, bt = _paged_setup(rows, 2, 128, lens, nb, seed=71)
+    qi = _rand(rows, H * 64, seed=72)
+    wi = torch.rand(rows, H, device=DEV)
+    rseq = torch.arange(rows, dtype=torch.int32, device=DEV)
+    rctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    c = ops.ctx(DEV)
+    scores = torch.empty(rows, L, device=DEV)
+    _native.C().dsa_scores(qi, wi, H, icache, bt, rseq, rctx, scores, c.status)
+    sref = dsa.index_scores_ref(qi.cpu(), wi.cpu(), icache.cpu(), bt.cpu(), rseq.cpu(), rctx.cpu(), H, L)
+    fin = torch.isfinite(sref)
+    torch.testing.assert_close(scores.cpu()[fin], sref[fin], rtol=1e-3, atol=1e-3)
+    k = 512
+    sel = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    n = torch.empty(rows, dtype=torch.int32, device=DEV)
+    _native.C().dsa_topk(scores, rctx, k, sel, n)
+    iref, nref = dsa.topk_ref(scores.cpu(), rctx.cpu(), k)
+    assert torch.equal(n.cpu(), nref)
+    for r in range(rows):
+        assert set(sel[r, :n[r]].tolist()) == set(iref[r, :nref[r]].tolist())
+    Hq = 8
+    q = _rand(rows, Hq * 128, seed=73)
+    out = torch.empty(rows, Hq * 128, dtype=torch.bfloat16, device=DEV)
+    _native.C().dsa_attention(q, kc, vc, bt, rseq, sel, n, out, Hq, 0.088)
+    oref = dsa.sparse_attention_ref(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), rseq.cpu(), sel.cpu(), n.cpu(), Hq, 0.088)
+    _close(out.cpu(), oref)
