@@ -77,6 +77,16 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout=5.0):
+        """Block until nvidia-smi has produced its first sample (it needs ~0.5 s to start)."""
+        t = time.monotonic()
+        while self.proc is not None and not self.lines and time.monotonic() - t < timeout:
+            time.sleep(0.05)
+
+    def mark(self):
+        """Samples before this point are warm-up; keep the last one as the clock at the region start."""
+        self.start_idx = max(len(self.lines) - 1, 0)
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -87,7 +97,7 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "start_idx", 0):]:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -193,11 +203,13 @@ def main():
     e2e_tps = B * a.steps / e2e_s
     # (4) device-driven decode steps, CUDA-event timed
     clocks = ClockSampler(local)
+    clocks.start()
     h = eng.begin_multi_decode(a.warmup + a.steps)
     for _ in range(a.warmup):
         eng.multi_decode_step(h)
+    clocks.wait_first()
     barrier()
-    clocks.start()
+    clocks.mark()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(a.steps):
@@ -232,8 +244,13 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        # Captured decode graphs hold NCCL work; tearing the communicator down
+        # under them can block, so ranks leave together after a final barrier.
+        torch.cuda.synchronize()
         dist.barrier()
-        dist.destroy_process_group()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     return 0
 
 

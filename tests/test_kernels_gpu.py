@@ -250,7 +250,7 @@ def test_dsa_kernels():
     from openmini_v1_b200.models import dsa
     rows, H, L = 5, 4, 1500
     lens = [1500, 1024, 700, 1, 1300]
-    nb = 200
+    nb = 320
     icache = _rand(nb, 16, 64, seed=70)
     kc, vc, bt = _paged_setup(rows, 2, 128, lens, nb, seed=71)
     qi = _rand(rows, H * 64, seed=72)
