@@ -49,6 +49,8 @@ def _args():
     p.add_argument("--out-tokens", type=int, default=512)
     p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; not the metric)")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--tp-transport", default="symm", choices=["symm", "nccl"],
+                   help="symm: fused reduce/RMSNorm/all-gather over peer memory; nccl: all-reduce baseline")
     return p.parse_args()
 
 
@@ -154,6 +156,9 @@ def main():
     model = DecoderLM(cfg, par=par, device=dev, seed=a.seed, weight_format=a.quant)
     if world > 1:
         model.set_comm(make_tp_comm(par, dev))
+        if a.tp_transport == "symm":
+            from openmini_v1_b200.parallel.symm import make_sp
+            model.set_sp(make_sp(par, dev, max_rows=4096, dim=cfg.hidden_size))
     torch.cuda.synchronize()
     init_s = time.monotonic() - t_init
     eng = LLMEngine(model, EngineConfig(max_num_seqs=B, max_num_batched_tokens=16384, max_model_len=max_len,
@@ -231,7 +236,8 @@ def main():
         "impl": "native",
         "config": {"model": cfg.name + (f"-L{cfg.num_layers}" if a.layers else ""), "quant": a.quant,
                    "global_batch": B, "seq_len": f"prompt U[{a.prompt_min},{a.prompt_max}] + {a.out_tokens} out",
-                   "parallelism": f"tp{world}", "temperature": 0.7, "top_p": 0.9,
+                   "parallelism": f"tp{world}", "tp_transport": a.tp_transport if world > 1 else None,
+                   "temperature": 0.7, "top_p": 0.9,
                    "l2": "inputs larger than L2 (weights streamed per step >> 126 MB); no flush"},
         "ttft_p50_ms": round(ttft_p50 * 1e3, 2), "tpot_p50_ms": round(ms_per_step, 4),
         "tpot_e2e_ms": round(e2e_s / a.steps * 1e3, 4), "prefill_s": round(prefill_s, 3),

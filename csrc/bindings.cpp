@@ -43,11 +43,25 @@ void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
 void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor icache, torch::Tensor bt,
                    torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor scores, torch::Tensor status);
 void om_dsa_topk(torch::Tensor scores, torch::Tensor row_ctx, int64_t k, torch::Tensor out_idx, torch::Tensor out_n);
+void om_flash_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                      torch::Tensor row_ctx, torch::Tensor tiles, torch::Tensor out, int64_t Hq, double scale,
+                      torch::Tensor status);
 void om_dsa_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor bt,
                       torch::Tensor row_seq, torch::Tensor sel, torch::Tensor sel_n, torch::Tensor out, int64_t Hq,
                       double scale);
 
 #include "common/om_host.h"
+
+int64_t om_symm_alloc(int64_t bytes);
+void om_symm_free(int64_t ptr);
+torch::Tensor om_symm_handle(int64_t ptr);
+int64_t om_symm_open(torch::Tensor handle);
+void om_symm_close(int64_t ptr);
+torch::Tensor om_symm_view(int64_t ptr, int64_t offset, std::vector<int64_t> shape, int64_t dtype_code);
+void om_sp_signal(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
+void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::Tensor h, torch::Tensor w,
+                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status);
+void om_sp_wait(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", [] { return (int64_t)om::g_launches.load(); }, "kernel launches issued so far");
@@ -70,6 +84,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_write", &om_kv_write);
   m.def("paged_attention", &om_paged_attention);
   m.def("paged_attention_tc", &om_paged_attention_tc, "tcgen05 paged decode attention (head_dim 128)");
+  m.def("flash_prefill", &om_flash_prefill, "tcgen05 causal FlashAttention prefill over the paged cache");
   m.def("paged_attention_workspace", &om_paged_attention_workspace);
   m.def("sample", &om_sample, py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("top_k"),
         py::arg("rng"), py::arg("out_tok"), py::arg("out_logprob") = py::none(),
@@ -84,4 +99,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dsa_scores", &om_dsa_scores, "DSA indexer scores over the paged indexer-key cache");
   m.def("dsa_topk", &om_dsa_topk, "per-row top-k key positions");
   m.def("dsa_attention", &om_dsa_attention, "attention over selected keys of the paged cache");
+  m.def("symm_alloc", &om_symm_alloc, "device buffer for peer mapping (zeroed)");
+  m.def("symm_free", &om_symm_free);
+  m.def("symm_handle", &om_symm_handle, "CUDA IPC handle bytes of a symm_alloc buffer");
+  m.def("symm_open", &om_symm_open, "map a peer's buffer from its IPC handle");
+  m.def("symm_close", &om_symm_close);
+  m.def("symm_view", &om_symm_view, "tensor view into a buffer (dtype 0 bf16, 1 fp32, 2 int32)");
+  m.def("sp_signal", &om_sp_signal, "publish this rank's partials for the next epoch");
+  m.def("sp_reduce_norm_gather", &om_sp_reduce_norm_gather,
+        "sum peer partials into own residual rows, RMSNorm, push normed rows to every rank");
+  m.def("sp_wait", &om_sp_wait, "wait until every rank pushed its normed rows for this epoch");
 }

@@ -13,12 +13,12 @@
 // instead of 2.
 //
 // Three independent shared-memory rings keep the weight stream deep:
-//   raw ring  packed weight tiles (+ Q4 scales), up to 18 slots, filled by the
-//             weight producer, emptied by the dequant warp that expands them
+//   raw ring  packed weight tiles (+ Q4 scales), up to 24 slots, filled by the
+//             weight producer, emptied once all dequant warps have read them
 //   x ring    activation tiles (128-byte swizzle), filled by the activation
 //             producer, emptied by the MMA
 //   w ring    bf16 operand tiles, written by the dequant warps, emptied by the MMA
-// so an activation reload never waits behind a weight slot and ~50-70 KB of
+// so an activation reload never waits behind a weight slot and ~80-110 KB of
 // packed weights stay in flight per SM.
 //
 // Roles (512 threads, one CTA per SM):
@@ -27,10 +27,10 @@
 //   warp 1       MMA issuer (one elected lane), 2 TMEM accumulators
 //   warp 2       TMEM allocation
 //   warps 4..7   epilogue (shared with the bf16 kernel)
-//   warps 8..    dequant warps; warp d expands every NDQ-th K block and owns the
-//                raw and w slots congruent to d (mod NDQ), so each warp consumes
-//                its own slots strictly in order and never waits on a barrier
-//                two phases ahead of its producer.
+//   warps 8..15  dequant warps; all eight expand every tile together (16 rows
+//                each, one 32-value half row per lane), so the latency from a raw
+//                tile landing to its bf16 operand being ready is one eighth of a
+//                tile's work and a 4-deep operand ring covers the MMA round trip.
 //
 // SWAP = true (decode): A = weight tile (M = 128 weight rows), B = activations
 // (N = BX tokens); the epilogue writes Y[token][row]. SWAP = false (prefill):
@@ -57,15 +57,13 @@ struct WqCfg {
   static constexpr int RAW_Q = QT == WQ_Q4 ? 128 * 32 : 128 * 64;
   static constexpr int RAW_S = QT == WQ_Q4 ? 2 * 128 * 2 : 0;
   static constexpr int RAW_BYTES = RAW_Q + RAW_S;  // multiple of 16
-  static constexpr int NDQ = BX <= 64 ? 5 : (BX == 128 ? 4 : 3);  // dequant warps = w-ring depth
-  static constexpr int WD = NDQ;
-  static constexpr int X_BUDGET = BX <= 128 ? 64 * 1024 : 96 * 1024;
-  static constexpr int XD_ = X_BUDGET / X_BYTES;
-  static constexpr int XD = XD_ > 16 ? 16 : (XD_ < 2 ? 2 : XD_);
-  static constexpr int RAW_AVAIL = 200 * 1024 - WD * W_BYTES - XD * X_BYTES;
-  static constexpr int RD_ = RAW_AVAIL / RAW_BYTES > 18 ? 18 : RAW_AVAIL / RAW_BYTES;
-  static constexpr int RD = (RD_ / NDQ) * NDQ;  // multiple of NDQ (private slots per warp)
-  static_assert(RD >= NDQ, "raw ring must hold one slot per dequant warp");
+  static constexpr int NDQ = 8;                   // dequant warps, 16 rows of every tile each
+  static constexpr int WD = 4;                    // bf16 operand ring
+  static constexpr int XD_ = (48 * 1024) / X_BYTES;
+  static constexpr int XD = XD_ > 8 ? 8 : (XD_ < 2 ? 2 : XD_);
+  static constexpr int RAW_AVAIL = 208 * 1024 - WD * W_BYTES - XD * X_BYTES;
+  static constexpr int RD = RAW_AVAIL / RAW_BYTES > 24 ? 24 : RAW_AVAIL / RAW_BYTES;
+  static_assert(RD >= 4, "raw ring too shallow");
   static constexpr int X_OFF = WD * W_BYTES;
   static constexpr int RAW_OFF = X_OFF + XD * X_BYTES;
   static constexpr int BAR_OFF = ((RAW_OFF + RD * RAW_BYTES + 15) / 16) * 16;
@@ -133,7 +131,7 @@ __global__ void __launch_bounds__(512, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WD; ++s) {
-      mbar_init(&w_ready[s], 1);
+      mbar_init(&w_ready[s], NDQ);
       mbar_init(&w_empty[s], 1);
     }
     for (int s = 0; s < XD; ++s) {
@@ -142,7 +140,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     for (int s = 0; s < RD; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 1);
+      mbar_init(&raw_empty[s], NDQ);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -231,57 +229,53 @@ __global__ void __launch_bounds__(512, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
+    // All NDQ warps expand every tile together: warp d owns rows [16d, 16d + 16),
+    // lane -> (row 16d + lane / 2, half lane % 2 of the 64 k values).
     const int d = warp - 8;
-    if (d < NDQ) {
-      int it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        int tr, tc, sp;
-        unit_coords(g, u, tr, tc, sp);
-        const int kb0 = sp * g.kb_per_split;
-        const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          if (it % NDQ != d) continue;
-          const int r = it % RD, s = it % WD;
-          if (!mbar_wait(&raw_full[r], (it / RD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
-          if (!mbar_wait(&w_empty[s], ((it / WD) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
-          const uint8_t* raw = rawbuf + r * C::RAW_BYTES;
-          uint8_t* st = wbuf + s * C::W_BYTES;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int row = lane + 32 * j;
-            uint8_t* wrow = st + row * 128;
-            const uint32_t sw = row & 7;
-            if (QT == WQ_Q4) {
-              const uint4 p0 = *reinterpret_cast<const uint4*>(raw + row * 32);
-              const uint4 p1 = *reinterpret_cast<const uint4*>(raw + row * 32 + 16);
-              const uint16_t* scp = reinterpret_cast<const uint16_t*>(raw + C::RAW_Q);
-              const uint32_t s0 = (uint32_t)scp[row] * 0x10001u;
-              const uint32_t s1 = (uint32_t)scp[128 + row] * 0x10001u;
-              *reinterpret_cast<uint4*>(wrow + ((0 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 0, s0);
-              *reinterpret_cast<uint4*>(wrow + ((1 ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 0, s0);
-              *reinterpret_cast<uint4*>(wrow + ((2 ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 4, s0);
-              *reinterpret_cast<uint4*>(wrow + ((3 ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 4, s0);
-              *reinterpret_cast<uint4*>(wrow + ((4 ^ sw) << 4)) = q4_chunk(p1.x, p1.y, 0, s1);
-              *reinterpret_cast<uint4*>(wrow + ((5 ^ sw) << 4)) = q4_chunk(p1.z, p1.w, 0, s1);
-              *reinterpret_cast<uint4*>(wrow + ((6 ^ sw) << 4)) = q4_chunk(p1.x, p1.y, 4, s1);
-              *reinterpret_cast<uint4*>(wrow + ((7 ^ sw) << 4)) = q4_chunk(p1.z, p1.w, 4, s1);
-            } else {
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const uint4 p = *reinterpret_cast<const uint4*>(raw + row * 64 + h * 16);
-                *reinterpret_cast<uint4*>(wrow + (((2 * h) ^ sw) << 4)) = i8_chunk(p.x, p.y);
-                *reinterpret_cast<uint4*>(wrow + (((2 * h + 1) ^ sw) << 4)) = i8_chunk(p.z, p.w);
-              }
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          // the raw slot is released only after the whole tile has been read
-          if (lane == 0) {
-            mbar_arrive(&w_ready[s]);
-            mbar_arrive(&raw_empty[r]);
-          }
+    const int row = d * 16 + (lane >> 1);
+    const int half = lane & 1;
+    const uint32_t sw = row & 7;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      int tr, tc, sp;
+      unit_coords(g, u, tr, tc, sp);
+      const int kb0 = sp * g.kb_per_split;
+      const int kb1 = min(g.num_kb, kb0 + g.kb_per_split);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int r = it % RD, s = it % WD;
+        if (!mbar_wait(&raw_full[r], (it / RD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
+        const uint8_t* raw = rawbuf + r * C::RAW_BYTES;
+        uint4 p0, p1;
+        uint32_t s2 = 0;
+        if (QT == WQ_Q4) {
+          // block `half` of the row: 16 bytes of nibbles (32 values) and its scale
+          p0 = *reinterpret_cast<const uint4*>(raw + row * 32 + half * 16);
+          s2 = (uint32_t)reinterpret_cast<const uint16_t*>(raw + C::RAW_Q)[half * 128 + row] * 0x10001u;
+        } else {
+          p0 = *reinterpret_cast<const uint4*>(raw + row * 64 + half * 32);
+          p1 = *reinterpret_cast<const uint4*>(raw + row * 64 + half * 32 + 16);
+        }
+        if (!mbar_wait(&w_empty[s], ((it / WD) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
+        uint8_t* wrow = wbuf + s * C::W_BYTES + row * 128;
+        const uint32_t c0 = 4 * half;
+        if (QT == WQ_Q4) {
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 0, s2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 0, s2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = q4_chunk(p0.x, p0.y, 4, s2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = q4_chunk(p0.z, p0.w, 4, s2);
+        } else {
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = i8_chunk(p0.x, p0.y);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = i8_chunk(p0.z, p0.w);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = i8_chunk(p1.x, p1.y);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = i8_chunk(p1.z, p1.w);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        // the raw slot is released only after every lane has read its part
+        if (lane == 0) {
+          mbar_arrive(&w_ready[s]);
+          mbar_arrive(&raw_empty[r]);
         }
       }
     }

@@ -48,16 +48,6 @@ __device__ __forceinline__ float block_max(float v, float* sh) {
   return sh[32];
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  f[0] = bf16lo(u.x); f[1] = bf16hi(u.x); f[2] = bf16lo(u.y); f[3] = bf16hi(u.y);
-  f[4] = bf16lo(u.z); f[5] = bf16hi(u.z); f[6] = bf16lo(u.w); f[7] = bf16hi(u.w);
-}
-__device__ __forceinline__ uint4 pack8(const float* f) {
-  uint4 u;
-  u.x = pack_bf16x2(f[0], f[1]); u.y = pack_bf16x2(f[2], f[3]);
-  u.z = pack_bf16x2(f[4], f[5]); u.w = pack_bf16x2(f[6], f[7]);
-  return u;
-}
 
 // out = rmsnorm(x [+ delta]) * w ; if delta != null, x is updated in place to x + delta.
 // D % 8 == 0, D <= 8 * NT * VPT.

@@ -217,6 +217,24 @@ class LLMEngine:
         return any(r.params.repetition_penalty != 1.0 or r.params.return_sampling_mask or r.params.return_routing
                    for r in rows_req)
 
+    @staticmethod
+    def _prefill_tiles(so, chunks, T):
+        """Query tiles for the tensor-core prefill attention: <= 128 consecutive rows of one
+        sequence each, as (row_start, rows, seq, keys of the last row), longest first.
+        Only prefill batches with enough rows get tiles (decode rows use the split-KV kernel)."""
+        if so.kind == "decode" or T < 128:
+            return []
+        tiles = []
+        o = 0
+        for si, c in enumerate(chunks):
+            n = c.end - c.start
+            for t0 in range(0, n, 128):
+                rows = min(128, n - t0)
+                tiles.append((o + t0, rows, si, c.start + t0 + rows))
+            o += n
+        tiles.sort(key=lambda x: -x[3])
+        return tiles
+
     def _build(self, so):
         """Stage metadata on pinned host memory and copy it to the device (one H2D per dtype)."""
         chunks = so.chunks
@@ -224,7 +242,8 @@ class LLMEngine:
         T = sum(c.end - c.start for c in chunks)
         mb = self.max_blocks_per_seq
         nL = sum(1 for c in chunks if c.wants_logits)
-        n_i32 = 5 * T + S * mb + nL
+        tiles = self._prefill_tiles(so, chunks, T)
+        n_i32 = 5 * T + S * mb + nL + 4 * len(tiles)
         st = self.stage
         if st.i32.numel() < n_i32:
             st.i32 = torch.empty(2 * n_i32, dtype=torch.int32, pin_memory=st.pin)
@@ -248,14 +267,18 @@ class LLMEngine:
                 logits_rows.append(o - 1)
                 rows_req.append(r)
         self.bm.fill_block_tables([c.req.seq_id for c in chunks], bt)
-        buf[5 * T + S * mb:n_i32] = logits_rows
+        o_t = 5 * T + S * mb + nL
+        buf[5 * T + S * mb:o_t] = logits_rows
+        if tiles:
+            buf[o_t:n_i32] = np.asarray(tiles, dtype=np.int32).reshape(-1)
         d = st.i32[:n_i32].to(self.device, non_blocking=True)
         st.h2d_bytes = n_i32 * 4
         fb = ForwardBatch(
             input_ids=d[0:T], positions=d[T:2 * T], slots=d[2 * T:3 * T], row_seq=d[3 * T:4 * T],
             row_ctx=d[4 * T:5 * T], block_tables=d[5 * T:5 * T + S * mb].view(S, mb),
             max_ctx=(self.cfg.max_model_len if so.kind == "decode" else max(c.end for c in chunks)),
-            logits_idx=d[5 * T + S * mb:n_i32])
+            logits_idx=d[5 * T + S * mb:o_t],
+            prefill_tiles=d[o_t:n_i32].view(-1, 4) if tiles else None)
         # sampling knobs
         B = len(rows_req)
         f = st.f32.numpy()

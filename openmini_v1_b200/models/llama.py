@@ -48,6 +48,8 @@ class ForwardBatch:
     # RL replay: per-MoE-layer forced expert ids [T, top_k] (None = route normally)
     forced_routing: dict | None = None
     record_routing: dict | None = None
+    # prefill query tiles [n, 4] int32 (row_start, rows, seq, keys of the last row) or None
+    prefill_tiles: torch.Tensor | None = None
 
 
 @dataclass
@@ -84,6 +86,7 @@ class DecoderLM(nn.Module):
         self.weight_format = weight_format
         self.layers = []
         self._comm = None
+        self._sp = None
         if materialize:
             self.init_random(seed, init_std)
 
@@ -103,8 +106,10 @@ class DecoderLM(nn.Module):
         cfg = self.cfg
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed * 1000003 + self.par.tp_rank)
+        shared = torch.Generator(device=self.device)  # replicated tensors are equal on every TP rank
+        shared.manual_seed(seed * 1000003 + 999983)
         D = cfg.hidden_size
-        self.embed = self._randn(gen, cfg.vocab_size, D, std=std)
+        self.embed = self._randn(shared, cfg.vocab_size, D, std=std)
         self.norm = torch.ones(D, dtype=self.dtype, device=self.device)
         self.lm_head = self.embed if cfg.tie_embeddings else self._randn(gen, self.vocab_local, D, std=std)
         self.layers = []
@@ -117,7 +122,7 @@ class DecoderLM(nn.Module):
             }
             if cfg.moe.is_moe_layer(i):
                 E, Fe = cfg.moe.num_experts, cfg.moe.expert_ffn
-                L["router"] = self._randn(gen, E, D, std=std)
+                L["router"] = self._randn(shared, E, D, std=std)
                 L["experts_gate_up"] = [self._randn(gen, 2 * Fe, D, std=std) for _ in range(E)]
                 L["experts_down"] = [self._randn(gen, D, Fe, std=std) for _ in range(E)]
             else:
@@ -125,7 +130,7 @@ class DecoderLM(nn.Module):
                 L["down"] = self._randn(gen, D, self.ffn, std=std)
             if cfg.dsa.enabled:
                 from .dsa import init_indexer
-                L.update(init_indexer(self, gen, std))
+                L.update(init_indexer(self, shared, std))
             if self.weight_format != "bf16":
                 from .quantize import quantize_layer
                 quantize_layer(L, self.weight_format)
@@ -154,6 +159,15 @@ class DecoderLM(nn.Module):
         """Tensor-parallel transport with ``all_reduce(t)`` and ``all_gather(t, dim)``."""
         self._comm = comm
 
+    def set_sp(self, sp):
+        """Sequence-parallel transport (``parallel.symm``): token-sharded residual stream with
+        fused reduce / RMSNorm / all-gather events replacing the all-reduces."""
+        self._sp = sp
+
+    def _use_sp(self, T: int) -> bool:
+        return (self._sp is not None and self._sp.fits(T) and not self.cfg.dsa.enabled
+                and not any("router" in L for L in self.layers))
+
     def _tp_sum(self, t):
         if self.par.tp > 1:
             self._comm.all_reduce(t)
@@ -165,12 +179,52 @@ class DecoderLM(nn.Module):
 
     def forward(self, fb: ForwardBatch, kv: KVCache) -> torch.Tensor:
         """Returns final-normed hidden states of rows ``fb.logits_idx``: [S', D]."""
+        if self.par.tp > 1 and self._use_sp(fb.input_ids.shape[0]):
+            return self.forward_sp(fb, kv)
         h = self.embed_tokens(fb.input_ids)  # residual stream [T, D]
         delta = None
         for i, L in enumerate(self.layers):
             h, delta = self.layer_forward(i, L, h, delta, fb, kv)
         x = ops.rmsnorm(h, self.norm, self.cfg.rms_eps, delta=delta)
         return x.index_select(0, fb.logits_idx)
+
+    def forward_sp(self, fb: ForwardBatch, kv: KVCache) -> torch.Tensor:
+        """Tensor-parallel forward with the residual stream sharded by token rows.
+
+        Rank r keeps the residual of rows [r Tp/W, (r+1) Tp/W) (Tp = T padded to a
+        multiple of W). Every row-parallel GEMM writes its partial into the
+        transport's partials region; one event sums the partials of the owned rows,
+        updates the residual, applies the next RMSNorm and gathers the normed rows
+        of all ranks, which the next column-parallel GEMM reads whole."""
+        sp, cfg = self._sp, self.cfg
+        T = fb.input_ids.shape[0]
+        Tp = sp.padded(T)
+        ids = fb.input_ids
+        if Tp > T:
+            ids = torch.cat([ids, ids.new_zeros(Tp - T)])
+        h = self.embed_tokens(ids[sp.own_slice(Tp)]).contiguous()  # own residual rows
+        k = 0
+        x = sp.reduce_norm(k, h, self.layers[0]["attn_norm"], cfg.rms_eps, Tp, has_partial=False)
+        for i, L in enumerate(self.layers):
+            a = x[:T]
+            qkv = ops.linear(a, L["qkv"])
+            ops.rope_kv(qkv, fb.positions, fb.slots, kv.k[i], kv.v[i], self.inv_freq, self.hq, self.hkv, self.hd,
+                        cfg.rope_mode)
+            if fb.prefill_tiles is not None and self.hd == 128:
+                attn = ops.flash_prefill(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
+                                         fb.prefill_tiles, self.hq, self.scale)
+            else:
+                attn = ops.paged_attention(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
+                                           self.hq, self.scale, fb.max_ctx)
+            k += 1
+            ops.linear(attn.view(T, self.hq * self.hd), L["o"], out=sp.partial(k, Tp)[:T])
+            x = sp.reduce_norm(k, h, L["ffn_norm"], cfg.rms_eps, Tp, has_partial=True)
+            act = ops.silu_mul(ops.linear(x[:T], L["gate_up"]))
+            k += 1
+            ops.linear(act, L["down"], out=sp.partial(k, Tp)[:T])
+            w_next = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
+            x = sp.reduce_norm(k, h, w_next, cfg.rms_eps, Tp, has_partial=True)
+        return x[:T].index_select(0, fb.logits_idx)
 
     def layer_forward(self, i, L, h, delta, fb: ForwardBatch, kv: KVCache):
         cfg = self.cfg
@@ -182,6 +236,9 @@ class DecoderLM(nn.Module):
         if cfg.dsa.enabled:
             from .dsa import dsa_attention
             attn = dsa_attention(self, i, L, a, qkv, fb, kv)
+        elif fb.prefill_tiles is not None and self.hd == 128:
+            attn = ops.flash_prefill(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
+                                     fb.prefill_tiles, self.hq, self.scale)
         else:
             attn = ops.paged_attention(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx, self.hq,
                                        self.scale, fb.max_ctx)

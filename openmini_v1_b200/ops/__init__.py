@@ -196,6 +196,25 @@ def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, sca
     return out
 
 
+def flash_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, tiles, Hq, scale, out=None):
+    """Causal prefill attention of query tiles (consecutive rows of one sequence) over the
+    paged cache; on the GPU the tcgen05 FlashAttention kernel (head_dim 128)."""
+    T = row_seq.shape[0]
+    D = k_cache.shape[3]
+    if not q.is_cuda:
+        o = ref.paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, scale)
+        if out is not None:
+            out.copy_(o.reshape(out.shape))
+            return out
+        return o.reshape(T, Hq * D)
+    if out is None:
+        out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
+    c = ctx(q.device)
+    _native.C().flash_prefill(q.reshape(T, -1), k_cache, v_cache, block_tables, row_ctx, tiles, out.view(T, -1),
+                              Hq, float(scale), c.status)
+    return out
+
+
 def sample(logits, temperature, top_p, top_k, rng, want_mask=False):
     """Returns (tokens int32, logprob fp32, packed keep mask int32 [B, ceil(V/32)] or None)."""
     B, V = logits.shape

@@ -49,8 +49,15 @@ def _worker(rank, world, port, q):
             fb = ForwardBatch(toks, torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(2, **i32)[None],
                               torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T, torch.tensor([T - 1]))
             outs.append(m.logits(m(fb, kv)))
+        # sequence-parallel transport (token-sharded residual, fused reduce/norm/gather events)
+        from openmini_v1_b200.parallel.symm import make_sp
+        shard.set_sp(make_sp(par, "cpu", 64, cfg.hidden_size, dtype=torch.float32))
+        kv = shard.allocate_kv(2)
+        fb = ForwardBatch(toks, torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(2, **i32)[None],
+                          torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T, torch.tensor([T - 1]))
+        sp_out = shard.logits(shard(fb, kv))
         q.put((rank, t.tolist(), g.tolist(), rs.tolist(), b.tolist(), mx.tolist(),
-               float((outs[0] - outs[1]).abs().max())))
+               float((outs[0] - outs[1]).abs().max()), float((outs[0] - sp_out).abs().max())))
     finally:
         dist.destroy_process_group()
 
@@ -89,13 +96,14 @@ def test_gloo_collectives_and_tp_decoder():
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
-    for rank, t, g, rs, b, mx, tp_err in res:
+    for rank, t, g, rs, b, mx, tp_err, sp_err in res:
         assert t == [3.0] * 4
         assert g == [0, 0, 1, 1]
         assert rs == ([0.0, 3.0] if rank == 0 else [6.0, 9.0])
         assert b == [10]
         assert mx == [1.0]
         assert tp_err < 1e-4, tp_err
+        assert sp_err < 1e-4, sp_err
 
 
 def test_local_comm_threads():

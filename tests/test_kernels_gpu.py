@@ -277,3 +277,32 @@ def test_dsa_kernels():
     _native.C().dsa_attention(q, kc, vc, bt, rseq, sel, n, out, Hq, 0.088)
     oref = dsa.sparse_attention_ref(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), rseq.cpu(), sel.cpu(), n.cpu(), Hq, 0.088)
     _close(out.cpu(), oref)
+
+
+@pytest.mark.parametrize("Hq,Hkv,qstd", [(8, 1, 1.0), (64, 8, 1.0), (4, 4, 6.0)])
+def test_flash_prefill(Hq, Hkv, qstd):
+    from openmini_v1_b200.engine.engine import LLMEngine
+    chunks = [(0, 300), (200, 150), (0, 1), (1000, 129), (0, 1200)]  # (cached prefix, new rows)
+    lens = [s + n for s, n in chunks]
+    S = len(chunks)
+    nb = sum((l + 15) // 16 for l in lens) + 8
+    kc, vc, bt = _paged_setup(S, Hkv, 128, lens, nb, seed=80)
+    T = sum(n for _, n in chunks)
+    qkv = _rand(T, (Hq + 2 * Hkv) * 128, std=qstd, seed=81)
+    rseq = torch.cat([torch.full((n,), i, dtype=torch.int32) for i, (_, n) in enumerate(chunks)]).to(DEV)
+    rctx = torch.cat([torch.arange(s + 1, s + n + 1, dtype=torch.int32) for s, n in chunks]).to(DEV)
+
+    class _C:
+        def __init__(self, s, n):
+            self.start, self.end = s, s + n
+
+    class _SO:
+        kind = "prefill"
+
+    tiles = LLMEngine._prefill_tiles(_SO, [_C(s, n) for s, n in chunks], T)
+    tiles = torch.tensor(tiles, dtype=torch.int32, device=DEV)
+    out = ops.flash_prefill(qkv, kc, vc, bt, rseq, rctx, tiles, Hq, 1 / math.sqrt(128))
+    ops.check_status()
+    want = ref.paged_attention(qkv.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), rseq.cpu(), rctx.cpu(), Hq,
+                               1 / math.sqrt(128))
+    _close(out.cpu(), want.reshape(T, -1))
