@@ -83,17 +83,19 @@ __device__ bool sp_wait_all(const SpArgs& a, int off, int target, int code) {
   return true;
 }
 
-__global__ void sp_signal_kernel(const SpArgs a) {
+__global__ void sp_signal_kernel(const __grid_constant__ SpArgs a) {
   if (threadIdx.x != 0) return;
   int* ep = ctrl(a.base[a.rank], 128);
   const int e = *ep + 1;
   *ep = e;
   __threadfence_system();  // the partials written by the previous kernels precede the flag
-  for (int p = 0; p < a.world; ++p) st_release_sys(ctrl(a.base[p], 0) + a.rank, e);
+#pragma unroll
+  for (int p = 0; p < SP_MAX_WORLD; ++p)
+    if (p < a.world) st_release_sys(ctrl(a.base[p], 0) + a.rank, e);
 }
 
 template <int NT>
-__global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const SpArgs a) {
+__global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const __grid_constant__ SpArgs a) {
   __shared__ float red[NT / 32];
   __shared__ int go;
   const int e = *ctrl(a.base[a.rank], 128);
@@ -112,7 +114,9 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const SpArgs 
         float v[8];
         unpack8(reinterpret_cast<const uint4*>(hr)[c], v);
         if (a.p_off >= 0) {
-          for (int p = 0; p < a.world; ++p) {
+#pragma unroll
+          for (int p = 0; p < SP_MAX_WORLD; ++p) {
+            if (p >= a.world) break;
             const uint4 u = reinterpret_cast<const uint4*>(a.base[p] + a.p_off + g * a.D * 2)[c];
             float d[8];
             unpack8(u, d);
@@ -142,7 +146,9 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const SpArgs 
 #pragma unroll
         for (int t = 0; t < 8; ++t) v[t] = v[t] * inv * wf[t];
         const uint4 o = pack8(v);
-        for (int p = 0; p < a.world; ++p) reinterpret_cast<uint4*>(a.base[p] + a.x_off + g * a.D * 2)[c] = o;
+#pragma unroll
+        for (int p = 0; p < SP_MAX_WORLD; ++p)
+          if (p < a.world) reinterpret_cast<uint4*>(a.base[p] + a.x_off + g * a.D * 2)[c] = o;
       }
       __syncthreads();  // red[] reuse
     }
@@ -156,12 +162,14 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const SpArgs 
     if (t == gridDim.x - 1) {
       *ticket = 0u;
       __threadfence_system();
-      for (int p = 0; p < a.world; ++p) red_release_sys_add(ctrl(a.base[p], 64) + a.rank, 1);
+#pragma unroll
+      for (int p = 0; p < SP_MAX_WORLD; ++p)
+        if (p < a.world) red_release_sys_add(ctrl(a.base[p], 64) + a.rank, 1);
     }
   }
 }
 
-__global__ void sp_wait_kernel(const SpArgs a) {
+__global__ void sp_wait_kernel(const __grid_constant__ SpArgs a) {
   if (threadIdx.x != 0) return;
   const int e = *ctrl(a.base[a.rank], 128);
   sp_wait_all(a, 64, e, OM_ERR_WAIT_FULL);

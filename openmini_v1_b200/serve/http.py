@@ -43,7 +43,7 @@ def chat_prompt(messages) -> str:
 
 
 def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metrics | None = None,
-               config=None) -> FastAPI:
+               config=None, trainer_factory=None) -> FastAPI:
     app = FastAPI(title="openmini_v1_b200")
     metrics = metrics or Metrics()
     metrics.model_loaded.set(1)
@@ -258,4 +258,6 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
                                 status_code=501)
         app.add_api_route(path, _ni, methods=["POST"])
 
+    from .training_api import mount_training
+    mount_training(app, trainer_factory)
     return app
