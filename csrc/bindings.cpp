@@ -63,6 +63,13 @@ void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::T
                               double eps, int64_t p_off, int64_t x_off, torch::Tensor status);
 void om_sp_wait(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 
+void om_moe_route(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> forced, torch::Tensor ids,
+                  torch::Tensor wts, torch::Tensor counts);
+void om_moe_permute(torch::Tensor x, torch::Tensor ids, torch::Tensor counts, torch::Tensor offsets,
+                    torch::Tensor cursor, torch::Tensor row_of, torch::Tensor xp);
+void om_moe_combine(torch::Tensor yp, torch::Tensor row_of, torch::Tensor wts, torch::Tensor out, bool add);
+void om_grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor y, torch::Tensor status);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", [] { return (int64_t)om::g_launches.load(); }, "kernel launches issued so far");
   m.doc() = "openmini_v1_b200 sm_100a kernels";
@@ -99,6 +106,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dsa_scores", &om_dsa_scores, "DSA indexer scores over the paged indexer-key cache");
   m.def("dsa_topk", &om_dsa_topk, "per-row top-k key positions");
   m.def("dsa_attention", &om_dsa_attention, "attention over selected keys of the paged cache");
+  m.def("moe_route", &om_moe_route, "router top-k + softmax weights + per-expert counts");
+  m.def("moe_permute", &om_moe_permute, "expert offsets and expert-sorted copy of the activations");
+  m.def("moe_combine", &om_moe_combine, "weighted sum of the experts' rows back per token");
+  m.def("grouped_gemm", &om_grouped_gemm, "grouped tcgen05 GEMM over expert-sorted rows");
   m.def("symm_alloc", &om_symm_alloc, "device buffer for peer mapping (zeroed)");
   m.def("symm_free", &om_symm_free);
   m.def("symm_handle", &om_symm_handle, "CUDA IPC handle bytes of a symm_alloc buffer");

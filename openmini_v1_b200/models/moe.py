@@ -28,9 +28,56 @@ def route(router_logits: torch.Tensor, k: int, forced: torch.Tensor | None = Non
     return ids, w
 
 
+def _stacked(L):
+    """Experts' weights stacked [E, N, K] for the grouped GEMM (rebuilt when the lists change)."""
+    src = (L["experts_gate_up"], L["experts_down"])
+    if L.get("_stack_src") is not src:
+        L["_gu_stack"] = torch.stack(list(src[0])).contiguous()
+        L["_down_stack"] = torch.stack(list(src[1])).contiguous()
+        L["_stack_src"] = src
+    return L["_gu_stack"], L["_down_stack"]
+
+
+def moe_forward_device(model, layer_idx, L, x, fb):
+    """Graph-capturable MoE: device routing, expert-sorted rows, two grouped tcgen05 GEMMs, combine."""
+    from .. import _native
+    cfg = model.cfg.moe
+    T, D = x.shape
+    k, E = cfg.top_k, cfg.num_experts
+    C = _native.C()
+    dev = x.device
+    logits = ops.linear(x, L["router"])
+    forced = fb.forced_routing.get(layer_idx) if fb.forced_routing else None
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    C.moe_route(logits.contiguous(), k, forced.to(torch.int32).contiguous() if forced is not None else None,
+                ids, w, counts)
+    if fb.record_routing is not None:
+        fb.record_routing[layer_idx] = ids.clone()
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    cursor = torch.empty(E, dtype=torch.int32, device=dev)
+    row_of = torch.empty(T * k, dtype=torch.int32, device=dev)
+    xp = torch.empty(T * k, D, dtype=x.dtype, device=dev)
+    C.moe_permute(x.contiguous(), ids, counts, offsets, cursor, row_of, xp)
+    gu_w, down_w = _stacked(L)
+    status = ops.ctx(dev).status
+    gu = torch.empty(T * k, gu_w.shape[1], dtype=x.dtype, device=dev)
+    C.grouped_gemm(xp, gu_w, offsets, gu, status)
+    act = ops.silu_mul(gu)
+    yp = torch.empty(T * k, D, dtype=x.dtype, device=dev)
+    C.grouped_gemm(act.contiguous(), down_w, offsets, yp, status)
+    out = torch.empty(T, D, dtype=x.dtype, device=dev)
+    C.moe_combine(yp, row_of, w, out, False)
+    return out
+
+
 def moe_forward(model, layer_idx, L, x, fb):
     cfg = model.cfg.moe
     T, D = x.shape
+    if (x.is_cuda and isinstance(L["experts_gate_up"][0], torch.Tensor) and x.dtype == torch.bfloat16
+            and D % 64 == 0 and cfg.expert_ffn % 64 == 0 and cfg.num_experts <= 256 and cfg.top_k <= 8):
+        return moe_forward_device(model, layer_idx, L, x, fb)
     logits = ops.linear(x, L["router"])
     forced = fb.forced_routing.get(layer_idx) if fb.forced_routing else None
     ids, w = route(logits, cfg.top_k, forced)

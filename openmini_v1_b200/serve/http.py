@@ -260,4 +260,8 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
 
     from .training_api import mount_training
     mount_training(app, trainer_factory)
+    from .health import HealthChecker, mount_health
+    mount_health(app, HealthChecker(aengine))
+    from .middleware import apply_middlewares
+    apply_middlewares(app)
     return app

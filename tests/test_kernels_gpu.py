@@ -306,3 +306,36 @@ def test_flash_prefill(Hq, Hkv, qstd):
     want = ref.paged_attention(qkv.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), rseq.cpu(), rctx.cpu(), Hq,
                                1 / math.sqrt(128))
     _close(out.cpu(), want.reshape(T, -1))
+
+
+@pytest.mark.parametrize("T,E,k,forced", [(37, 8, 2, False), (300, 16, 2, False), (5, 4, 3, True)])
+def test_moe_device_path(T, E, k, forced):
+    from types import SimpleNamespace
+    from openmini_v1_b200.models import moe
+    D, F = 256, 128
+    x = _rand(T, D, seed=90)
+    L = {"router": _rand(E, D, std=0.2, seed=91),
+         "experts_gate_up": [_rand(2 * F, D, std=0.06, seed=100 + e) for e in range(E)],
+         "experts_down": [_rand(D, F, std=0.06, seed=200 + e) for e in range(E)]}
+    model = SimpleNamespace(cfg=SimpleNamespace(moe=SimpleNamespace(top_k=k, num_experts=E, expert_ffn=F)))
+    fr = {0: torch.randint(0, E, (T, k), device=DEV, dtype=torch.int32)} if forced else None
+    fb = SimpleNamespace(forced_routing=fr, record_routing={})
+    out = moe.moe_forward_device(model, 0, L, x, fb)
+    ops.check_status()
+    # fp32 statement of the same op
+    lg = (x.float() @ L["router"].float().t()).bfloat16().float()
+    if forced:
+        ids = fr[0].long()
+        sel = lg.gather(1, ids)
+    else:
+        sel, ids = torch.topk(lg, k, dim=-1)
+    w = torch.softmax(sel, -1)
+    assert torch.equal(fb.record_routing[0].long(), ids) or forced
+    want = torch.zeros(T, D, device=DEV)
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            gu = x[t].float() @ L["experts_gate_up"][e].float().t()
+            a = torch.nn.functional.silu(gu[:F]) * gu[F:]
+            want[t] += w[t, j] * (a.bfloat16().float() @ L["experts_down"][e].float().t())
+    _close(out, want)

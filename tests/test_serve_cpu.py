@@ -190,3 +190,51 @@ def test_incremental_decoder_utf8():
     ids = tok.encode("héllo ✓", add_bos=False)
     d = IncrementalDecoder(tok)
     assert "".join(d.push(i) for i in ids) == "héllo ✓"
+
+
+def test_health_middleware_errors_hardware(stack):
+    from openmini_v1_b200.errors import KVCacheExhausted, OpenMiniError
+    from openmini_v1_b200.hardware.detect import classify, detect_hardware, CpuInfo, GpuInfo
+    from openmini_v1_b200.serve.middleware import mask_sensitive_data
+    aeng, tok = stack[0], stack[1]
+    c = TestClient(create_app(aeng, tok, "tiny"))
+    assert c.get("/health/live").json() == {"status": "alive"}
+    r = c.get("/health/ready")
+    assert r.status_code in (200, 503) and {x["name"] for x in r.json()["components"]} >= {"gpu", "model"}
+    r = c.get("/health", headers={"x-request-id": "abc"})
+    assert r.headers["x-request-id"] == "abc"
+    assert "***MASKED***" in mask_sensitive_data("Bearer eyJhbGciOiJIUzI1NiJ9 api_key=sk-123")
+    assert "eyJ" not in mask_sensitive_data("Authorization: Bearer eyJhbGciOiJIUzI1NiJ9")
+    e = KVCacheExhausted("no blocks", code=7, need=3)
+    assert isinstance(e, OpenMiniError) and e.code == "ENG007" and e.http_status == 503
+    assert e.to_dict()["need"] == 3
+    hp = detect_hardware(nvml=None)
+    assert hp.cpu.cores_logical >= 1 and hp.level in ("cpu_only", "gpu_other", "blackwell", "blackwell_nvswitch")
+    g = [GpuInfo(i, "B200", (10, 0), 180 << 30, 148, 1965, 1000.0, 18) for i in range(8)]
+    assert classify(CpuInfo("x86_64", 8, 4), g, 0)[0] == "blackwell_nvswitch"
+
+
+class _FakeNVML:
+    NVML_CLOCK_SM = 1
+
+    class _Mem:
+        total = 183359 << 20
+
+    def nvmlInit(self): pass
+    def nvmlShutdown(self): pass
+    def nvmlDeviceGetCount(self): return 2
+    def nvmlDeviceGetHandleByIndex(self, i): return i
+    def nvmlDeviceGetName(self, h): return b"NVIDIA B200"
+    def nvmlDeviceGetCudaComputeCapability(self, h): return (10, 0)
+    def nvmlDeviceGetMemoryInfo(self, h): return self._Mem()
+    def nvmlDeviceGetNumGpuCores(self, h): return 148 * 128
+    def nvmlDeviceGetMaxClockInfo(self, h, t): return 1965
+    def nvmlDeviceGetEnforcedPowerLimit(self, h): return 1000000
+    def nvmlDeviceGetNvLinkState(self, h, l): return 1
+
+
+def test_hardware_detection_fake_nvml():
+    from openmini_v1_b200.hardware.detect import detect_hardware
+    hp = detect_hardware(nvml=_FakeNVML())
+    assert len(hp.gpus) == 2 and hp.gpus[0].sm_count == 148 and hp.gpus[0].nvlink_active == 18
+    assert hp.level == "blackwell" and hp.strategy["tp"] == 2
