@@ -46,6 +46,7 @@ class EngineConfig:
                                                              224, 256])
     eos_token_id: int | None = None
     seed: int = 0
+    speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
 
 
 class _Pinned:
@@ -77,6 +78,10 @@ class LLMEngine:
         self.requests: dict = {}
         self.stage = _Pinned(self.device)
         self.graphs = None
+        self.spec = None
+        if self.cfg.speculative_k > 0:
+            from .speculative import NgramProposer
+            self.spec = NgramProposer(self.cfg.speculative_k)
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "preemptions": 0}
         if self.is_cuda and self.cfg.use_cuda_graph:
             from .cuda_graph import DecodeGraphs
@@ -131,6 +136,10 @@ class LLMEngine:
         if so.kind == "decode":
             for c in so.chunks:
                 self._sync_bm_tokens(c.req)
+        if so.kind == "decode" and self.spec is not None:
+            from .speculative import eligible, spec_decode_step
+            if all(eligible(c.req) for c in so.chunks):
+                return spec_decode_step(self, so, self.spec)
         fb, samp, rows_req = self._build(so)
         want_routing = any(c.req.params.return_routing for c in so.chunks)
         if (so.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(so.chunks))

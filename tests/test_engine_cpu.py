@@ -85,3 +85,18 @@ def test_quant_reference_roundtrip():
     assert (d - w).abs().max() < 0.02 * 4 / 8 + 1e-3
     q8, s8 = ref.quantize_int8(w.bfloat16())
     assert (ref.dequant_int8(q8, s8).float() - w).abs().max() < 1e-3
+
+
+def test_speculative_ngram_matches_greedy():
+    from openmini_v1_b200.engine.speculative import NgramProposer
+    p = NgramProposer(3)
+    assert p.propose([1, 2, 3, 9, 1, 2]) == [3, 9, 1]
+    assert p.propose([5, 6, 7]) == []
+    m = DecoderLM(tiny(), device="cpu", seed=4)
+    pat = [11, 12, 13, 14, 15, 16, 17, 18] * 4
+    sp = SamplingParams(temperature=0.0, max_tokens=24, ignore_eos=True)
+    base = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256)).generate([pat, pat[:13]], sp)
+    e = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256, speculative_k=4))
+    spec = e.generate([pat, pat[:13]], sp)
+    assert [r.output_token_ids for r in spec] == [r.output_token_ids for r in base]
+    assert e.stats["spec_proposed"] > 0
