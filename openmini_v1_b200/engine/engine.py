@@ -47,6 +47,7 @@ class EngineConfig:
     eos_token_id: int | None = None
     seed: int = 0
     speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
+    preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)
 
 
 class _Pinned:
@@ -63,6 +64,21 @@ class _Pinned:
         self.d2h_bytes = 0
 
 
+class _RestoreOnly:
+    """Swap-in only (restored sessions) when preemption recomputes."""
+
+    def __init__(self, eng):
+        from .kv_swap import KVSwapper
+        self._sw = KVSwapper(eng)
+
+    def swap_out(self, r):
+        r.swapped = None
+        r.routing = {}
+
+    def swap_in(self, r):
+        return self._sw.swap_in(r)
+
+
 class LLMEngine:
     def __init__(self, model: DecoderLM, config: EngineConfig | None = None):
         self.model = model
@@ -76,6 +92,13 @@ class LLMEngine:
         self.sched = Scheduler(self.bm, self.cfg.max_num_seqs, self.cfg.max_num_batched_tokens,
                                self.cfg.max_model_len, self.cfg.enable_chunked_prefill)
         self.requests: dict = {}
+        self.swapper = None
+        from .kv_swap import KVSwapper
+        if self.cfg.preemption_mode == "swap":
+            self.swapper = KVSwapper(self)
+            self.sched.swapper = self.swapper
+        else:
+            self.sched.swapper = _RestoreOnly(self)
         self.stage = _Pinned(self.device)
         self.graphs = None
         self.spec = None

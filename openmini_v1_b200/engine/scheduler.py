@@ -49,6 +49,7 @@ class Scheduler:
         self.chunked = enable_chunked_prefill
         self.waiting: deque = deque()
         self.running: list = []
+        self.swapper = None  # KVSwapper: preempt by swapping KV to host instead of recompute
 
     # ------------------------------------------------------------ queue ops
     def add(self, req: Request):
@@ -87,9 +88,12 @@ class Scheduler:
 
     def _preempt(self, r: Request, out: SchedulerOutput):
         self.running.remove(r)
+        if self.swapper is not None:
+            self.swapper.swap_out(r)  # KV of the computed prefix kept on the host
+        else:
+            r.routing = {}  # recomputed from scratch on re-admission
         self.bm.free(r.seq_id)
         r.num_computed = 0
-        r.routing = {}  # recomputed from scratch on re-admission
         r.num_preemptions += 1
         r.status = RequestStatus.WAITING
         self.waiting.appendleft(r)
@@ -116,6 +120,11 @@ class Scheduler:
                 break
             self.waiting.popleft()
             cached = self.bm.allocate(r.seq_id, toks)
+            if getattr(r, "swapped", None) and self.swapper is not None:
+                n_sw = r.swapped[0]
+                if self.bm.seq_len(r.seq_id) >= n_sw:
+                    cached = max(cached, self.swapper.swap_in(r))
+            cached = min(cached, len(toks) - 1)  # the last token is always run (its logits are needed)
             r.num_computed = cached
             r.status = RequestStatus.RUNNING
             self.running.append(r)

@@ -100,3 +100,32 @@ def test_speculative_ngram_matches_greedy():
     spec = e.generate([pat, pat[:13]], sp)
     assert [r.output_token_ids for r in spec] == [r.output_token_ids for r in base]
     assert e.stats["spec_proposed"] > 0
+
+
+def test_swap_preemption_and_session_persistence(tmp_path):
+    from openmini_v1_b200.engine.kv_swap import restore_session, save_session
+    m = DecoderLM(tiny(), device="cpu", seed=2)
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, 32000, (30,), generator=g).tolist() for _ in range(3)]
+    sp = SamplingParams(temperature=0.0, max_tokens=20, ignore_eos=True)
+    e = LLMEngine(m, EngineConfig(max_num_seqs=3, max_model_len=128, num_blocks=9, enable_prefix_cache=False,
+                                  preemption_mode="swap"))
+    outs = e.generate(prompts, sp)
+    assert e.stats["preemptions"] > 0 and e.swapper.swap_ins > 0
+    e2 = LLMEngine(m, EngineConfig(max_num_seqs=3, max_model_len=128, num_blocks=64))
+    assert [r.output_token_ids for r in outs] == [r.output_token_ids for r in e2.generate(prompts, sp)]
+    # session: 8 tokens, save, restore in a fresh engine, 8 more == 16 uninterrupted
+    full = LLMEngine(m, EngineConfig(max_num_seqs=1, max_model_len=128)).generate(
+        [prompts[0]], SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True))[0].output_token_ids
+    a = LLMEngine(m, EngineConfig(max_num_seqs=1, max_model_len=128))
+    r = a.add_request("s", prompts[0], SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
+    while r.status.name not in ("FINISHED",):
+        a.step()
+        if len(r.output_token_ids) == 7:
+            save_session(a, r, str(tmp_path / "sess.safetensors"))
+    b = LLMEngine(m, EngineConfig(max_num_seqs=1, max_model_len=128))
+    r2 = restore_session(b, str(tmp_path / "sess.safetensors"), "s2",
+                         SamplingParams(temperature=0.0, max_tokens=9, ignore_eos=True))
+    while r2.status.name != "FINISHED":
+        b.step()
+    assert r.output_token_ids[:7] + r2.output_token_ids == full
