@@ -75,6 +75,9 @@ def moe_forward_device(model, layer_idx, L, x, fb):
 def moe_forward(model, layer_idx, L, x, fb):
     cfg = model.cfg.moe
     T, D = x.shape
+    ep = getattr(model, "_ep", None)
+    if ep is not None and ep.size > 1:  # expert parallel: all-to-all dispatch / combine
+        return ep.forward(model, layer_idx, L, x, fb)
     if (x.is_cuda and isinstance(L["experts_gate_up"][0], torch.Tensor) and x.dtype == torch.bfloat16
             and D % 64 == 0 and cfg.expert_ffn % 64 == 0 and cfg.num_experts <= 256 and cfg.top_k <= 8):
         return moe_forward_device(model, layer_idx, L, x, fb)
