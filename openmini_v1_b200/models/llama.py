@@ -87,6 +87,7 @@ class DecoderLM(nn.Module):
         self.layers = []
         self._comm = None
         self._sp = None
+        self._ep = None
         if materialize:
             self.init_random(seed, init_std)
 
@@ -159,6 +160,15 @@ class DecoderLM(nn.Module):
         """Tensor-parallel transport with ``all_reduce(t)`` and ``all_gather(t, dim)``."""
         self._comm = comm
 
+    def set_ep(self, ep, ep_rank: int | None = None):
+        """Expert parallelism (``parallel.expert.ExpertParallel``): keep only this rank's
+        experts in every MoE layer and route their tokens with all-to-all."""
+        from ..parallel.expert import shard_experts
+        self._ep = ep
+        if ep is not None and ep.size > 1:
+            r = ep.rank if ep_rank is None else ep_rank
+            self.layers = [shard_experts(L, ep.size, r) if "router" in L else L for L in self.layers]
+
     def set_sp(self, sp):
         """Sequence-parallel transport (``parallel.symm``): token-sharded residual stream with
         fused reduce / RMSNorm / all-gather events replacing the all-reduces."""
@@ -193,7 +203,8 @@ class DecoderLM(nn.Module):
 
         Rank r keeps the residual of rows [r Tp/W, (r+1) Tp/W) (Tp = T padded to a
         multiple of W). Every row-parallel GEMM writes its partial into the
-        transport's partials region; one event sums the partials of the owned rows,
+        transport's partials region (on the GPU: straight into the owner ranks'
+        slots from the GEMM epilogue); one event sums the partials of the owned rows,
         updates the residual, applies the next RMSNorm and gathers the normed rows
         of all ranks, which the next column-parallel GEMM reads whole."""
         sp, cfg = self._sp, self.cfg
@@ -217,11 +228,11 @@ class DecoderLM(nn.Module):
                 attn = ops.paged_attention(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
                                            self.hq, self.scale, fb.max_ctx)
             k += 1
-            ops.linear(attn.view(T, self.hq * self.hd), L["o"], out=sp.partial(k, Tp)[:T])
+            sp.linear_rs(attn.view(T, self.hq * self.hd), L["o"], k, Tp)
             x = sp.reduce_norm(k, h, L["ffn_norm"], cfg.rms_eps, Tp, has_partial=True)
             act = ops.silu_mul(ops.linear(x[:T], L["gate_up"]))
             k += 1
-            ops.linear(act, L["down"], out=sp.partial(k, Tp)[:T])
+            sp.linear_rs(act, L["down"], k, Tp)
             w_next = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
             x = sp.reduce_norm(k, h, w_next, cfg.rms_eps, Tp, has_partial=True)
         return x[:T].index_select(0, fb.logits_idx)
