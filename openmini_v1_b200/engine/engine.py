@@ -138,6 +138,27 @@ class LLMEngine:
     def has_unfinished(self) -> bool:
         return self.sched.has_unfinished()
 
+    def take_unfinished(self) -> list:
+        """Remove every unfinished request (KV freed) and return the Request objects,
+        generated tokens included, for another engine to ``adopt``."""
+        out = []
+        for r in list(self.sched.running) + list(self.sched.waiting):
+            self.sched.abort(r.request_id)
+            self.requests.pop(r.request_id, None)
+            out.append(r)
+        return out
+
+    def adopt(self, req: Request) -> Request:
+        """Continue a request taken from another engine: its prompt and generated tokens
+        are re-prefilled here (fresh KV) and decoding resumes where it stopped."""
+        from .request import _ids
+        req.seq_id = next(_ids)
+        req.num_computed = 0
+        req.routing = {}
+        self.sched.add(req)
+        self.requests[req.request_id] = req
+        return req
+
     def generate(self, prompts, params=None) -> list:
         """Run prompts (lists of token ids) to completion; returns Requests in input order."""
         reqs = []
