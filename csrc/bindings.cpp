@@ -3,11 +3,11 @@
 
 void om_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> resid,
              c10::optional<torch::Tensor> workspace, torch::Tensor status, int64_t force_swap,
-             int64_t force_splits);
+             int64_t force_splits, std::vector<int64_t> peer);
 std::vector<int64_t> om_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, bool allow_split);
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
-                torch::Tensor status, int64_t force_swap, int64_t force_splits);
+                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer);
 void om_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w, torch::Tensor out,
                 double eps);
 void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, torch::Tensor out,
@@ -60,7 +60,7 @@ void om_symm_close(int64_t ptr);
 torch::Tensor om_symm_view(int64_t ptr, int64_t offset, std::vector<int64_t> shape, int64_t dtype_code);
 void om_sp_signal(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::Tensor h, torch::Tensor w,
-                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status);
+                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push);
 void om_sp_wait(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 
 void om_moe_route(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> forced, torch::Tensor ids,
@@ -75,12 +75,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "openmini_v1_b200 sm_100a kernels";
   m.def("gemm", &om_gemm, "bf16 tcgen05 GEMM: out = x @ w^T (+ resid)", py::arg("x"), py::arg("w"),
         py::arg("out"), py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
-        py::arg("force_swap") = -1, py::arg("force_splits") = 0);
+        py::arg("force_swap") = -1, py::arg("force_splits") = 0, py::arg("peer") = std::vector<int64_t>{});
   m.def("gemm_plan", &om_gemm_plan);
   m.def("gemm_wq", &om_gemm_wq, "weight-only quantised tcgen05 GEMM (0 = Q4 block-32, 1 = INT8 per row)",
         py::arg("x"), py::arg("qtiles"), py::arg("scales"), py::arg("qtype"), py::arg("out"),
         py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
-        py::arg("force_swap") = -1, py::arg("force_splits") = 0);
+        py::arg("force_swap") = -1, py::arg("force_splits") = 0, py::arg("peer") = std::vector<int64_t>{});
   m.def("rmsnorm", &om_rmsnorm, py::arg("x"), py::arg("delta"), py::arg("w"), py::arg("out"), py::arg("eps"));
   m.def("layernorm", &om_layernorm);
   m.def("silu_mul", &om_silu_mul);
@@ -118,6 +118,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_view", &om_symm_view, "tensor view into a buffer (dtype 0 bf16, 1 fp32, 2 int32)");
   m.def("sp_signal", &om_sp_signal, "publish this rank's partials for the next epoch");
   m.def("sp_reduce_norm_gather", &om_sp_reduce_norm_gather,
-        "sum peer partials into own residual rows, RMSNorm, push normed rows to every rank");
+        "sum peer partials into own residual rows, RMSNorm, push normed rows to every rank",
+        py::arg("bases"), py::arg("rank"), py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("p_off"),
+        py::arg("x_off"), py::arg("status"), py::arg("push") = false);
   m.def("sp_wait", &om_sp_wait, "wait until every rank pushed its normed rows for this epoch");
 }

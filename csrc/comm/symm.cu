@@ -8,7 +8,8 @@
 //
 // Buffer layout (identical on every rank):
 //   [0, 256)    control words: ready[8] (offset 0), agdone[8] (offset 64),
-//               epoch (offset 128), CTA ticket (offset 132)
+//               epoch (offset 128), CTA ticket of sp_reduce (offset 132),
+//               CTA ticket of the peer-output GEMM (offset 136)
 //   [256, ...)  data regions addressed by byte offset (partials and gathered
 //               activations, double-buffered by the caller)
 //
@@ -24,7 +25,15 @@
 //   sp_wait     wait agdone[p] >= epoch for all p (the gathered activations are
 //               complete); the next column-parallel GEMM reads them locally
 // so reduce-scatter, residual add, RMSNorm and all-gather are one kernel and
-// each byte crosses NVLink once. Every wait is bounded (OM_WAIT_LIMIT_NS) and
+// each byte crosses NVLink once.
+//
+// Push variant (the default of the decoder): the row-parallel GEMM itself
+// stores each output tile straight into the owner rank's partials slot
+// ([world][rows_own][D], slot = source rank) as it leaves TMEM, and its last
+// CTA publishes ready[me] = epoch on every rank (gemm_common.cuh PeerOut /
+// peer_publish). The GEMM -> reduce-scatter is then one kernel whose NVLink
+// transfer overlaps the remaining tiles' math, sp_signal is not launched, and
+// sp_reduce (push = 1) sums the W slots from local memory. Every wait is bounded (OM_WAIT_LIMIT_NS) and
 // records an error code instead of hanging.
 //
 // Reference counterpart: the tensor-parallel row split -> all_reduce and column
@@ -47,6 +56,8 @@ struct SpArgs {
   int D;
   long long p_off;              // partials region offset (-1: no reduction, normalise only)
   long long x_off;              // gathered normed-activation region offset
+  int push;                     // 1: the partials were pushed into this rank's slots by the
+                                // peer-output GEMM ([world][rows_own][D] at p_off, local reads)
   __nv_bfloat16* h;             // own residual rows [rows_own, D]
   const __nv_bfloat16* w;       // RMSNorm weight [D]
   float eps;
@@ -117,7 +128,9 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const __grid_
 #pragma unroll
           for (int p = 0; p < SP_MAX_WORLD; ++p) {
             if (p >= a.world) break;
-            const uint4 u = reinterpret_cast<const uint4*>(a.base[p] + a.p_off + g * a.D * 2)[c];
+            const uint8_t* src = a.push ? a.base[a.rank] + a.p_off + ((size_t)p * a.rows_own + r) * a.D * 2
+                                        : a.base[p] + a.p_off + g * a.D * 2;
+            const uint4 u = reinterpret_cast<const uint4*>(src)[c];
             float d[8];
             unpack8(u, d);
 #pragma unroll
@@ -241,7 +254,7 @@ void om_sp_signal(std::vector<int64_t> bases, int64_t rank, torch::Tensor status
 // h: own residual rows [rows_own, D] (updated in place when p_off >= 0);
 // normed rows land at x_off + global_row * D * 2 of every rank's buffer.
 void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::Tensor h, torch::Tensor w,
-                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status) {
+                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push) {
   TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2, "sp_reduce: h");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.numel() == h.size(1), "sp_reduce: w");
   const int D = h.size(1);
@@ -251,6 +264,7 @@ void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::T
   a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   a.eps = eps;
+  a.push = push ? 1 : 0;
   const int grid = std::max<int>(1, std::min<int>(a.rows_own, 2 * om::num_sms()));
   om::sp_reduce_norm_gather_kernel<256><<<grid, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(a);
   OM_LAUNCH_CHECK();

@@ -78,6 +78,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on a phase parity. Returns false (and records `code`) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -91,6 +102,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
         return false;
       }
       if (status && *(volatile int*)status != 0) return false;  // someone else already failed
+    }
+  }
+}
+// Same, with a suspend-time hint: a waiting thread may sleep up to `hint_ns`
+// inside try_wait instead of spinning (fewer issue slots burnt while waiting).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns, int* status,
+                                                int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if ((++spins & 15u) == 0) {
+      if (globaltimer() - t0 > OM_WAIT_LIMIT_NS) {
+        record_error(status, code);
+        return false;
+      }
+      if (status && *(volatile int*)status != 0) return false;
     }
   }
 }
@@ -123,6 +152,24 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Shared-space loads / stores by 32-bit shared address (no generic-address
+// translation, short-scoreboard latency).
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -7,9 +7,13 @@
 
 namespace om {
 
+// Sums the split-K partials, applies the optional per-column scale and
+// residual, and stores bf16 rows locally or, with po.pworld > 0, into the
+// owner rank's partials slot over NVLink followed by the epoch publication
+// (the split-K form of the fused GEMM -> reduce-scatter).
 __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int Ym, int Yn,
                                      __nv_bfloat16* __restrict__ Y, int ldo, const __nv_bfloat16* resid,
-                                     const float* __restrict__ col_scale) {
+                                     const float* __restrict__ col_scale, const PeerOut po) {
   const size_t plane = (size_t)Ym * Yn;
   const int nv = Yn >> 2;  // float4 groups per row (Yn % 4 == 0 checked on host)
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)Ym * nv;
@@ -20,7 +24,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
       float4 p = *reinterpret_cast<const float4*>(P + s * plane + (size_t)m * Yn + n);
       acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
     }
-    __nv_bfloat16* y = Y + (size_t)m * ldo + n;
+    __nv_bfloat16* y = (po.pworld > 0 ? peer_row(po, ldo, m) : Y + (size_t)m * ldo) + n;
     if (col_scale) {
       acc.x *= col_scale[n]; acc.y *= col_scale[n + 1]; acc.z *= col_scale[n + 2]; acc.w *= col_scale[n + 3];
     }
@@ -33,6 +37,11 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
     o.x = pack_bf16x2(acc.x, acc.y);
     o.y = pack_bf16x2(acc.z, acc.w);
     *reinterpret_cast<uint2*>(y) = o;
+  }
+  if (po.pworld > 0) {
+    __threadfence_system();
+    __syncthreads();
+    peer_publish(po);
   }
 }
 
@@ -49,6 +58,22 @@ static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   }
   gemm_bf16_tc_kernel<BN><<<grid, 256, C::SMEM_BYTES, st>>>(ta, tb, g);
   OM_LAUNCH_CHECK();
+}
+
+bool peer_from_list(const std::vector<int64_t>& v, int M, PeerOut& po) {
+  po = PeerOut{};
+  if (v.empty()) return false;
+  const int world = (int)v.size() - 3;
+  if (world < 1 || world > 8) throw std::runtime_error("peer output: 1..8 rank bases expected");
+  po.peer_off = v[0];
+  po.rows_own = (int)v[1];
+  po.prank = (int)v[2];
+  po.pworld = world;
+  if (po.rows_own <= 0 || (long long)po.rows_own * world < M || po.prank < 0 || po.prank >= world ||
+      po.peer_off % 16 != 0)
+    throw std::runtime_error("peer output: bad rows_own / rank / offset");
+  for (int i = 0; i < world; ++i) po.peer[i] = reinterpret_cast<uint8_t*>(v[3 + i]);
+  return true;
 }
 
 GemmPlan plan_gemm(int M, int N, int K, int sms, bool allow_split, int force_swap) {
@@ -90,7 +115,7 @@ static void set_splits(GemmPlan& p, int s, int sms) {
 
 void run_gemm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, int M, int N, int K,
               __nv_bfloat16* out, int ldo, const __nv_bfloat16* resid, float* workspace, size_t ws_bytes,
-              int* status, int force_swap, int force_splits, cudaStream_t st) {
+              int* status, int force_swap, int force_splits, cudaStream_t st, const PeerOut* po) {
   const int sms = num_sms();
   GemmPlan p = plan_gemm(M, N, K, sms, workspace != nullptr, force_swap);
   if (force_splits > 0 && workspace) set_splits(p, force_splits, sms);
@@ -104,7 +129,7 @@ void run_gemm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, 
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, p.cols, ldb, 64, p.bn,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  GemmArgs g;
+  GemmArgs g{};
   g.rows = p.rows;
   g.cols = p.cols;
   g.num_kb = p.num_kb;
@@ -124,6 +149,7 @@ void run_gemm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, 
     g.epi = resid ? EPI_RESID : EPI_STORE;
     g.out = out;
     g.resid = resid;
+    if (po) g.po = *po;
   }
   switch (p.bn) {
     case 32: launch_bn<32>(ta, tb, g, p.grid, st); break;
@@ -131,15 +157,16 @@ void run_gemm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, 
     case 128: launch_bn<128>(ta, tb, g, p.grid, st); break;
     default: launch_bn<256>(ta, tb, g, p.grid, st); break;
   }
-  if (p.splits > 1) launch_splitk_reduce(workspace, p.splits, M, N, out, ldo, resid, nullptr, st);
+  if (p.splits > 1) launch_splitk_reduce(workspace, p.splits, M, N, out, ldo, resid, nullptr, st, po);
 }
 
 void launch_splitk_reduce(const float* ws, int splits, int M, int N, __nv_bfloat16* out, int ldo,
-                          const __nv_bfloat16* resid, const float* col_scale, cudaStream_t st) {
+                          const __nv_bfloat16* resid, const float* col_scale, cudaStream_t st, const PeerOut* po) {
   const int nthreads = 256;
   const size_t work = (size_t)M * (N / 4);
   const int blocks = (int)std::min<size_t>((work + nthreads - 1) / nthreads, (size_t)num_sms() * 8);
-  splitk_reduce_kernel<<<blocks, nthreads, 0, st>>>(ws, splits, M, N, out, ldo, resid, col_scale);
+  PeerOut pz{};
+  splitk_reduce_kernel<<<blocks, nthreads, 0, st>>>(ws, splits, M, N, out, ldo, resid, col_scale, po ? *po : pz);
   OM_LAUNCH_CHECK();
 }
 
@@ -148,7 +175,7 @@ void launch_splitk_reduce(const float* ws, int splits, int M, int N, __nv_bfloat
 // ------------------------------------------------------------------ torch op
 void om_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> resid,
              c10::optional<torch::Tensor> workspace, torch::Tensor status, int64_t force_swap,
-             int64_t force_splits) {
+             int64_t force_splits, std::vector<int64_t> peer) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "om_gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16,
@@ -169,12 +196,15 @@ void om_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<
     ws = workspace->data_ptr<float>();
     ws_bytes = workspace->numel() * sizeof(float);
   }
+  om::PeerOut po;
+  const bool has_peer = om::peer_from_list(peer, M, po);
+  TORCH_CHECK(!has_peer || !resid.has_value(), "om_gemm: peer output takes no residual");
   if (M == 0) return;
   om::run_gemm(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
                reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), w.stride(0), M, N, K,
                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rp, ws, ws_bytes,
                status.data_ptr<int>(), (int)force_swap, (int)force_splits,
-               at::cuda::getCurrentCUDAStream().stream());
+               at::cuda::getCurrentCUDAStream().stream(), has_peer ? &po : nullptr);
 }
 
 std::vector<int64_t> om_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, bool allow_split) {

@@ -9,6 +9,46 @@ namespace om {
 
 enum GemmEpi : int { EPI_STORE = 0, EPI_RESID = 1, EPI_PARTIAL = 2 };
 
+// Peer output (tensor-parallel GEMM -> reduce-scatter in one kernel). With
+// pworld > 0, row m of Y goes to the owner rank o = m / rows_own, into slot
+// `prank` of its partials region: peer[o] + peer_off + ((prank * rows_own +
+// m % rows_own) * ldo + n) * 2 bytes, stored over NVLink (plain st.global to a
+// CUDA-IPC mapping of the peer's buffer) as the tile leaves TMEM. The last CTA
+// to finish then publishes the epoch (peer_publish).
+struct PeerOut {
+  uint8_t* peer[8];
+  long long peer_off;
+  int rows_own, prank, pworld;
+};
+
+__device__ __forceinline__ __nv_bfloat16* peer_row(const PeerOut& p, int ldo, int m) {
+  const int o = m / p.rows_own;
+  const int lr = m - o * p.rows_own;
+  return reinterpret_cast<__nv_bfloat16*>(p.peer[o] + p.peer_off) + (size_t)(p.prank * p.rows_own + lr) * ldo;
+}
+
+// End-of-kernel publication of a peer-output kernel. Control words of the
+// symmetric buffer (byte offsets): ready[8] at 0, epoch at 128, GEMM ticket at
+// 136. Every thread has fenced its peer stores at system scope before the CTA
+// barrier that precedes this call; thread 0 of the last CTA bumps the epoch
+// and writes ready[prank] = epoch on every rank with release semantics.
+__device__ __forceinline__ void peer_publish(const PeerOut& po) {
+  if (po.pworld <= 0 || threadIdx.x != 0) return;
+  uint8_t* own = po.peer[po.prank];
+  unsigned* ticket = reinterpret_cast<unsigned*>(own + 136);
+  const unsigned t = atomicAdd(ticket, 1u);
+  if (t != gridDim.x - 1) return;
+  *ticket = 0u;
+  int* ep = reinterpret_cast<int*>(own + 128);
+  const int e = *ep + 1;
+  *ep = e;
+  __threadfence_system();
+  for (int p = 0; p < po.pworld; ++p) {
+    int* f = reinterpret_cast<int*>(po.peer[p]) + po.prank;
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+  }
+}
+
 struct GemmArgs {
   int rows;          // MMA M extent (rows of A)
   int cols;          // MMA N extent (rows of B)
@@ -24,7 +64,18 @@ struct GemmArgs {
   const uint8_t* wtiles;       // quantised weights, pre-tiled (weight-only GEMM)
   int ldo;           // leading dimension of Y / resid (elements)
   int* status;
+  int dbg;           // profiling knobs of the weight-only kernel (0 in production)
+  int rgroup;        // weight-only SWAP: weight row-tiles per unit (tiles_r counts groups)
+  int wt_tiles;      // weight-only: number of 128-row weight tiles
+  int chunk;         // weight-only: K blocks per copy chunk (divides num_kb and kb_per_split)
+  PeerOut po;        // peer output (po.pworld > 0), see PeerOut
 };
+
+// Row pointer of output row m (local Y, or the owner's slot in peer mode).
+__device__ __forceinline__ __nv_bfloat16* out_row(const GemmArgs& g, int m) {
+  if (g.po.pworld > 0) return peer_row(g.po, g.ldo, m);
+  return reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ldo;
+}
 
 __device__ __forceinline__ void unit_coords(const GemmArgs& g, int u, int& tr, int& tc, int& sp) {
   sp = u % g.splits;
@@ -78,9 +129,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
     }
     return;
   }
-  __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(g.out);
   if (!g.swap) {
-    __nv_bfloat16* dst = Y + (size_t)r * g.ldo + c0;
+    __nv_bfloat16* dst = out_row(g, r) + c0;
     const __nv_bfloat16* rs = g.resid ? g.resid + (size_t)r * g.ldo + c0 : nullptr;
     if (ncol == 32 && (g.ldo & 7) == 0) {
 #pragma unroll
@@ -112,10 +162,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (j < ncol) {
-        const size_t o = (size_t)(c0 + j) * g.ldo + r;
         float t = f[j];
-        if (g.epi == EPI_RESID) t += __bfloat162float(g.resid[o]);
-        Y[o] = __float2bfloat16_rn(t);
+        if (g.epi == EPI_RESID) t += __bfloat162float(g.resid[(size_t)(c0 + j) * g.ldo + r]);
+        out_row(g, c0 + j)[r] = __float2bfloat16_rn(t);
       }
     }
   }

@@ -163,7 +163,9 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
 
+  if (g.po.pworld > 0) __threadfence_system();  // peer-output stores of this thread
   __syncthreads();
+  peer_publish(g.po);
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -1,4 +1,5 @@
 // Host launcher of the weight-only-quantised tcgen05 GEMM (Q4 block-32 / INT8 per row).
+#include <cstdlib>
 #include "../common/om_host.h"
 #include "gemm_launch.h"
 #include "gemm_wq.cuh"
@@ -7,7 +8,7 @@ namespace om {
 
 template <int BX, int QT, bool SWAP>
 static void launch_wq(const CUtensorMap& tx, const GemmArgs& g, int grid, cudaStream_t st) {
-  using C = WqCfg<BX, QT>;
+  using C = WqCfg<BX, QT, SWAP>;
   static bool attr_set[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -40,7 +41,7 @@ static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g
 // scales: INT8 only, fp32 [N] per-row scale (applied in the epilogue).
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
-                torch::Tensor status, int64_t force_swap, int64_t force_splits) {
+                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_wq: x");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.dim() == 2, "gemm_wq: out");
   const int M = x.size(0), K = x.size(1), N = out.size(1);
@@ -60,42 +61,72 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
   const int rows = swap ? N : M, cols = swap ? M : N;
   const int bx = swap ? (M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256) : 128;
   const int bn_mma = swap ? bx : 128;
-  om::GemmArgs g;
+  om::GemmArgs g{};
+  om::PeerOut po;
+  const bool has_peer = om::peer_from_list(peer, M, po);
+  TORCH_CHECK(!has_peer || !resid.has_value(), "gemm_wq: peer output takes no residual");
   g.rows = rows;
   g.cols = cols;
-  g.tiles_r = (rows + 127) / 128;
+  const int wt_tiles = (N + 127) / 128;  // 128-row weight tiles
+  g.wt_tiles = wt_tiles;
   g.tiles_c = (cols + bn_mma - 1) / bn_mma;
   g.num_kb = K / 64;
-  const int units = g.tiles_r * g.tiles_c;
-  int splits = 1;
+  int splits = 1, rgroup = 1;
   float* ws = nullptr;
   size_t ws_bytes = 0;
   if (workspace.has_value()) {
     ws = workspace->data_ptr<float>();
     ws_bytes = workspace->numel() * sizeof(float);
   }
-  if (ws && N % 4 == 0) {
-    if (force_splits > 0) {
-      splits = (int)force_splits;
-    } else {
-      // smallest split count whose work units fill the persistent grid's rounds
-      // to within 6% (each split keeps >= 8 K blocks)
-      double best = 1e30;
-      for (int s = 1; s <= 16 && g.num_kb / s >= 8; ++s) {
-        const int u = units * s;
-        const double rounds = (double)((u + sms - 1) / sms);
-        const double waste = rounds * sms / u;
-        if (waste < best * 0.94) {
-          best = waste;
-          splits = s;
+  // Plan (decode / SWAP): choose the weight row-tiles per unit R (activation reuse) and
+  // the split-K factor s by a byte-count model of the busiest SM: rounds of units x
+  // bytes each unit streams (R packed weight tiles + one activation tile per kb), plus
+  // the fp32 partials of split-K (written and re-read, spread over the SMs).
+  const int raw_bytes = qtype == 0 ? 4608 : 8192;
+  const int x_bytes = bx * 64 * 2;
+  const int rmax = swap ? std::max(1, 256 / bn_mma) : 1;
+  const bool can_split = ws && N % 4 == 0;
+  const size_t max_split_ws = can_split ? std::max<size_t>(1, ws_bytes / ((size_t)M * N * sizeof(float))) : 1;
+  if (force_splits > 0 && can_split) {
+    splits = std::min<int>((int)force_splits, g.num_kb);
+    rgroup = rmax;
+    while (rgroup > 1 && (wt_tiles + rgroup - 1) / rgroup * g.tiles_c * splits < sms) rgroup >>= 1;
+  } else {
+    double best = 1e300;
+    for (int R = 1; R <= rmax; R <<= 1) {
+      const int groups = swap ? (wt_tiles + R - 1) / R : (rows + 127) / 128;
+      for (int sc = 1; sc <= (can_split ? 16 : 1); ++sc) {
+        if (sc > 1 && (g.num_kb / sc < 4 || (size_t)sc > max_split_ws)) break;
+        const int kbps = (g.num_kb + sc - 1) / sc;
+        const long long units = (long long)groups * g.tiles_c * sc;
+        const long long rounds = (units + sms - 1) / sms;
+        const double unit_bytes = (double)kbps * (std::min(R, wt_tiles) * raw_bytes + x_bytes);
+        double cost = rounds * unit_bytes;
+        if (sc > 1) cost += 2.0 * sc * (double)M * N * 4 / sms;
+        if (cost < best * 0.98) {
+          best = cost;
+          splits = sc;
+          rgroup = R;
         }
       }
     }
-    splits = std::min<int>(splits, g.num_kb);
-    splits = std::min<int>(splits, (int)std::max<size_t>(1, ws_bytes / ((size_t)M * N * sizeof(float))));
   }
-  const int kbps = (g.num_kb + splits - 1) / splits;
+  static const int env_r = [] { const char* e = std::getenv("OM_WQ_R"); return e ? std::atoi(e) : 0; }();
+  static const int env_s = [] { const char* e = std::getenv("OM_WQ_S"); return e ? std::atoi(e) : 0; }();
+  static const int env_c = [] { const char* e = std::getenv("OM_WQ_CHUNK"); return e ? std::atoi(e) : 0; }();
+  if (env_r > 0) rgroup = std::min(env_r, rmax);
+  if (env_s > 0 && can_split) splits = std::min(env_s, g.num_kb);
+  g.rgroup = swap ? rgroup : 1;
+  g.tiles_r = swap ? (wt_tiles + g.rgroup - 1) / g.rgroup : (rows + 127) / 128;
+  const int units = g.tiles_r * g.tiles_c;
+  // copy chunk: the largest power of two <= the kernel's CHMAX dividing the K blocks
+  const int chmax = swap ? (bx <= 64 ? 4 : bx <= 128 ? 2 : 1) : 2;
+  int chunk = env_c > 0 ? std::min(env_c, chmax) : chmax;
+  while (chunk > 1 && g.num_kb % chunk) chunk >>= 1;
+  int kbps = (g.num_kb + splits - 1) / splits;
+  kbps = (kbps + chunk - 1) / chunk * chunk;
   splits = (g.num_kb + kbps - 1) / kbps;
+  g.chunk = chunk;
   g.splits = splits;
   g.kb_per_split = kbps;
   g.swap = swap ? 1 : 0;
@@ -103,6 +134,11 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
   g.ldo = out.stride(0);
   g.wscale = qtype == 1 ? scales->data_ptr<float>() : nullptr;
   g.wtiles = qtiles.data_ptr<uint8_t>();
+  static const int dbg_env = [] {
+    const char* e = std::getenv("OM_WQ_DBG");
+    return e ? std::atoi(e) : 0;
+  }();
+  g.dbg = dbg_env;
   const __nv_bfloat16* rp = resid.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
   if (resid.has_value())
     TORCH_CHECK(resid->sizes() == out.sizes() && resid->stride(0) == out.stride(0), "gemm_wq: resid layout");
@@ -114,9 +150,12 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
     g.out = out.data_ptr();
     g.resid = rp;
+    if (has_peer) g.po = po;
   }
-  CUtensorMap tx = om::make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, x.stride(0), 64, bx,
-                                    CU_TENSOR_MAP_SWIZZLE_128B);
+  // activations as [K/64][M][64]: a box {64, bx, chunk} is `chunk` swizzled [bx][64] tiles
+  TORCH_CHECK(x.stride(0) % 8 == 0, "gemm_wq: x row stride must be a multiple of 8 elements");
+  CUtensorMap tx = om::make_tmap_3d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, K / 64, x.stride(0), 64,
+                                    64, bx, chunk, CU_TENSOR_MAP_SWIZZLE_128B);
   const int grid = std::min(units * splits, sms);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   if (qtype == 0)
@@ -125,5 +164,5 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     om::dispatch<om::WQ_I8>(bx, swap, tx, g, grid, st);
   if (splits > 1)
     om::launch_splitk_reduce(ws, splits, M, N, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rp,
-                             qtype == 1 ? scales->data_ptr<float>() : nullptr, st);
+                             qtype == 1 ? scales->data_ptr<float>() : nullptr, st, has_peer ? &po : nullptr);
 }

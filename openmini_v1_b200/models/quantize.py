@@ -107,14 +107,14 @@ class Q4Weight:
     def nbytes(self):
         return self.tiles.numel()
 
-    def linear(self, x, out=None, resid=None):
+    def linear(self, x, out=None, resid=None, peer=None):
         if not x.is_cuda:
             y = ref.linear(x, self.dequantize().to(x.dtype), resid)
             if out is not None:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.tiles, None, 0, self.shape[0], out, resid)
+        return _wq_linear(x, self.tiles, None, 0, self.shape[0], out, resid, peer)
 
 
 class Int8Weight:
@@ -159,7 +159,7 @@ class Int8Weight:
     def nbytes(self):
         return self.tiles.numel() + self.scale.numel() * 4
 
-    def linear(self, x, out=None, resid=None):
+    def linear(self, x, out=None, resid=None, peer=None):
         if not x.is_cuda:
             y = (x.float() @ self.qweight.float().t()) * self.scale
             if resid is not None:
@@ -169,10 +169,10 @@ class Int8Weight:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid)
+        return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid, peer)
 
 
-def _wq_linear(x, tiles, scale, qtype, N, out, resid):
+def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
@@ -181,7 +181,10 @@ def _wq_linear(x, tiles, scale, qtype, N, out, resid):
     c = ops.ctx(x.device)
     ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status)
+    if peer is not None:
+        _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status, peer=peer)
+    else:
+        _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status)
     return out
 
 

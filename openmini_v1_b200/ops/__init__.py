@@ -76,9 +76,17 @@ def check_status(device=None):
 GEMM_WS_FLOATS = 64 << 20
 
 
-def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, resid: torch.Tensor | None = None):
-    """y = x @ w^T (+ resid). ``w`` is a bf16 [N, K] tensor or a quantised weight object."""
+def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+           peer: list | None = None):
+    """y = x @ w^T (+ resid). ``w`` is a bf16 [N, K] tensor or a quantised weight object.
+
+    ``peer`` (CUDA only) = [partials byte offset, rows per rank, this rank, base pointer of
+    every rank]: output row m is stored into rank m // rows_per_rank's symmetric buffer
+    (slot of this rank) over NVLink and the kernel publishes the epoch when done; ``out``
+    then only supplies the row stride."""
     if not isinstance(w, torch.Tensor):
+        if peer is not None:
+            return w.linear(x, out=out, resid=resid, peer=peer)
         return w.linear(x, out=out, resid=resid)
     if not x.is_cuda:
         y = ref.linear(x, w, resid)
@@ -98,7 +106,10 @@ def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, resid: torch.Ten
     c = ctx(x.device)
     ws = c.workspace("gemm", GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    _native.C().gemm(x2, w, o2, r2, ws, c.status)
+    if peer is not None:
+        _native.C().gemm(x2, w, o2, r2, ws, c.status, peer=peer)
+    else:
+        _native.C().gemm(x2, w, o2, r2, ws, c.status)
     return out
 
 

@@ -13,7 +13,14 @@ partial output into this rank's *partials* region; one event then
   3. waits until every rank's normed rows have arrived (``sp_wait``),
 
 after which the next column-parallel GEMM (QKV, gate-up, LM head) reads the full
-normed activations locally. Reduce-scatter, residual add, RMSNorm and
+normed activations locally.
+
+With ``push=True`` (the default) step 1 and the NVLink half of step 2 move into
+the row-parallel GEMM (``linear_rs``): its epilogue stores every output tile
+into the owner rank's partials slot over NVLink as the tile leaves TMEM and its
+last CTA publishes the epoch, so GEMM and reduce-scatter are one kernel whose
+transfer overlaps the remaining tiles' math; the reduce then sums W local
+slots. Reduce-scatter, residual add, RMSNorm and
 all-gather are one kernel; every byte crosses NVLink once. Regions are
 double-buffered by event parity; the flag protocol (every event waits for every
 rank's signal of the same event) keeps a fast rank from overwriting a region a
@@ -62,7 +69,8 @@ class _SPBase:
 class SymmetricSP(_SPBase):
     """Peer-mapped buffers + fused reduce / RMSNorm / all-gather kernels (one process per GPU)."""
 
-    def __init__(self, group, device, max_rows: int, dim: int):
+    def __init__(self, group, device, max_rows: int, dim: int, push: bool = True):
+        self.push = push
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -101,14 +109,27 @@ class SymmetricSP(_SPBase):
     def gathered(self, k: int, rows: int) -> torch.Tensor:
         return _native.C().symm_view(self.ptr, self._off("x", k), [rows, self.dim], 0)
 
+    def linear_rs(self, x: torch.Tensor, w, k: int, Tp: int):
+        """Row-parallel GEMM of event ``k`` whose output rows land in their owners' partials
+        slots (push mode: fused GEMM -> reduce-scatter; otherwise a local partial)."""
+        from .. import ops
+        T = x.shape[0]
+        out = self.partial(k, Tp)[:T]
+        if not self.push:
+            return ops.linear(x, w, out=out)
+        peer = [self._off("p", k), Tp // self.world, self.rank, *self.bases]
+        return ops.linear(x, w, out=out, peer=peer)
+
     def reduce_norm(self, k: int, h_own: torch.Tensor, w: torch.Tensor, eps: float, Tp: int,
                     has_partial: bool) -> torch.Tensor:
         from .. import ops
         C = _native.C()
         status = ops.ctx(self.device).status
-        C.sp_signal(self.bases, self.rank, status)
+        pushed = has_partial and self.push
+        if not pushed:  # a peer-output GEMM published this event itself
+            C.sp_signal(self.bases, self.rank, status)
         C.sp_reduce_norm_gather(self.bases, self.rank, h_own, w, float(eps),
-                                self._off("p", k) if has_partial else -1, self._off("x", k), status)
+                                self._off("p", k) if has_partial else -1, self._off("x", k), status, pushed)
         C.sp_wait(self.bases, self.rank, status)
         return self.gathered(k, Tp)
 
@@ -141,6 +162,10 @@ class EmulatedSP(_SPBase):
     def gathered(self, k: int, rows: int) -> torch.Tensor:
         return self._x[k & 1][:rows]
 
+    def linear_rs(self, x: torch.Tensor, w, k: int, Tp: int):
+        from .. import ops
+        return ops.linear(x, w, out=self.partial(k, Tp)[:x.shape[0]])
+
     def reduce_norm(self, k: int, h_own: torch.Tensor, w: torch.Tensor, eps: float, Tp: int,
                     has_partial: bool) -> torch.Tensor:
         own = self.own_slice(Tp)
@@ -161,11 +186,11 @@ class EmulatedSP(_SPBase):
         pass
 
 
-def make_sp(par, device, max_rows: int, dim: int, dtype=torch.bfloat16):
+def make_sp(par, device, max_rows: int, dim: int, dtype=torch.bfloat16, push: bool = True):
     """The sequence-parallel transport for this tensor-parallel group (None when tp == 1)."""
     if par.tp == 1:
         return None
     dev = torch.device(device)
     if dev.type == "cuda":
-        return SymmetricSP(par.tp_group, dev, max_rows, dim)
+        return SymmetricSP(par.tp_group, dev, max_rows, dim, push=push)
     return EmulatedSP(par.tp_group, dev, max_rows, dim, dtype)

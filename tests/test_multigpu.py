@@ -1,7 +1,8 @@
 """Tensor parallelism on 2+ GPUs (one process per GPU, NCCL): the sequence-
 parallel transport over peer memory (fused reduce / RMSNorm / all-gather
 kernels) gives the same logits as the NCCL all-reduce path, eagerly and under
-CUDA-graph replay. Skipped on machines with fewer than two GPUs."""
+CUDA-graph replay, with the row-parallel GEMMs fused with the reduce-scatter
+(peer-output epilogue) and without. Skipped on machines with fewer than two GPUs."""
 import os
 import socket
 
@@ -20,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, wfmt, push):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -37,7 +38,7 @@ def _worker(rank, world, port, q):
         par = ParallelState.build(tp=world)
         cfg = ModelConfig(name="tp-test", vocab_size=1024, hidden_size=1024, num_layers=3, num_heads=8,
                           num_kv_heads=2, head_dim=128, intermediate_size=2048)
-        m = DecoderLM(cfg, par=par, device=dev, seed=3)
+        m = DecoderLM(cfg, par=par, device=dev, seed=3, weight_format=wfmt)
         m.set_comm(CollectiveOps(par.tp_group))
         T = 37
         i32 = dict(dtype=torch.int32, device=dev)
@@ -46,7 +47,7 @@ def _worker(rank, world, port, q):
                           torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T, torch.arange(T, device=dev))
         kv = m.allocate_kv(4)
         base = m.logits(m(fb, kv)).float()
-        m.set_sp(make_sp(par, dev, 256, cfg.hidden_size))
+        m.set_sp(make_sp(par, dev, 256, cfg.hidden_size, push=push))
         errs = []
         for _ in range(3):
             errs.append(float((m.logits(m(fb, kv)).float() - base).abs().max()))
@@ -71,12 +72,16 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sp_transport_matches_allreduce():
+@pytest.mark.parametrize("wfmt,push", [("bf16", True), ("bf16", False), ("q4", True)])
+def test_sp_transport_matches_allreduce(wfmt, push):
+    """push=True: the row-parallel GEMMs store their output tiles into the owner ranks'
+    partials slots over NVLink and publish the epoch themselves (fused GEMM ->
+    reduce-scatter); push=False: local partials pulled by the reduce kernel."""
     world = min(torch.cuda.device_count(), 4)
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, wfmt, push)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(world))
