@@ -55,6 +55,7 @@ struct PrefillArgs {
   int Hq, Hkv, G;
   int items;               // ntiles * Hq
   float scale_log2;
+  float* lse;              // optional [T, Hq] natural-log sum of exp of the scaled scores (ring merges)
   int* status;
 };
 
@@ -284,6 +285,8 @@ __global__ void __launch_bounds__(256, 1)
       if (!mbar_wait(&p_empty[last & 1], (last >> 1) & 1, status, OM_ERR_WAIT_ACCUM)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      if (a.lse != nullptr && t < tl.y)  // log-sum-exp of the row: (m_used + log2 l) in log2 units
+        a.lse[(size_t)(tl.x + t) * a.Hq + h] = l > 0.f ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
       __nv_bfloat16* orow = a.out + (size_t)(tl.x + t) * a.out_ld + h * 128;
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(256, 1)
 // device, rows of one tile belonging to one sequence and consecutive in q / out.
 void om_flash_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor row_ctx, torch::Tensor tiles, torch::Tensor out, int64_t Hq, double scale,
-                      torch::Tensor status) {
+                      torch::Tensor status, c10::optional<torch::Tensor> lse) {
   using namespace om::fa_pf;
   const int ntiles = tiles.size(0);
   if (ntiles == 0) return;
@@ -348,6 +351,13 @@ void om_flash_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   a.items = ntiles * Hq;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.status = status.data_ptr<int>();
+  a.lse = nullptr;
+  if (lse.has_value()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->is_contiguous() && lse->dim() == 2 &&
+                    lse->size(0) >= q.size(0) && lse->size(1) == Hq,
+                "flash_prefill: lse must be fp32 [T, Hq]");
+    a.lse = lse->data_ptr<float>();
+  }
   const uint64_t cache_rows = (uint64_t)k_cache.size(0) * Hkv * 16;
   CUtensorMap tk = om::make_tmap_2d(k_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, cache_rows, 128,
                                     64, 16, CU_TENSOR_MAP_SWIZZLE_128B);

@@ -45,7 +45,7 @@ void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor 
 void om_dsa_topk(torch::Tensor scores, torch::Tensor row_ctx, int64_t k, torch::Tensor out_idx, torch::Tensor out_n);
 void om_flash_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor row_ctx, torch::Tensor tiles, torch::Tensor out, int64_t Hq, double scale,
-                      torch::Tensor status);
+                      torch::Tensor status, c10::optional<torch::Tensor> lse);
 void om_dsa_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor bt,
                       torch::Tensor row_seq, torch::Tensor sel, torch::Tensor sel_n, torch::Tensor out, int64_t Hq,
                       double scale);
@@ -91,7 +91,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_write", &om_kv_write);
   m.def("paged_attention", &om_paged_attention);
   m.def("paged_attention_tc", &om_paged_attention_tc, "tcgen05 paged decode attention (head_dim 128)");
-  m.def("flash_prefill", &om_flash_prefill, "tcgen05 causal FlashAttention prefill over the paged cache");
+  m.def("flash_prefill", &om_flash_prefill, "tcgen05 causal FlashAttention prefill over the paged cache",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_tables"), py::arg("row_ctx"),
+        py::arg("tiles"), py::arg("out"), py::arg("Hq"), py::arg("scale"), py::arg("status"),
+        py::arg("lse") = py::none());
   m.def("paged_attention_workspace", &om_paged_attention_workspace);
   m.def("sample", &om_sample, py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("top_k"),
         py::arg("rng"), py::arg("out_tok"), py::arg("out_logprob") = py::none(),

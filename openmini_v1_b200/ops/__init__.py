@@ -207,9 +207,10 @@ def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, sca
     return out
 
 
-def flash_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, tiles, Hq, scale, out=None):
+def flash_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, tiles, Hq, scale, out=None, lse=None):
     """Causal prefill attention of query tiles (consecutive rows of one sequence) over the
-    paged cache; on the GPU the tcgen05 FlashAttention kernel (head_dim 128)."""
+    paged cache; on the GPU the tcgen05 FlashAttention kernel (head_dim 128). With ``lse``
+    (fp32 [T, Hq]) the natural-log sum-exp of every row's scaled scores is written too."""
     T = row_seq.shape[0]
     D = k_cache.shape[3]
     if not q.is_cuda:
@@ -222,7 +223,7 @@ def flash_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, tiles, Hq
         out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
     c = ctx(q.device)
     _native.C().flash_prefill(q.reshape(T, -1), k_cache, v_cache, block_tables, row_ctx, tiles, out.view(T, -1),
-                              Hq, float(scale), c.status)
+                              Hq, float(scale), c.status, lse=lse)
     return out
 
 
