@@ -60,6 +60,16 @@ class ModelConfig:
     moe: MoEConfig = field(default_factory=MoEConfig)
     dsa: DSAConfig = field(default_factory=DSAConfig)
     architecture: str = "llama"
+    # sliding-window attention (Gemma-style local layers): 0 = off; with a window,
+    # layer i is local unless (i + 1) % sliding_window_global_every == 0 (0: every layer local)
+    sliding_window: int = 0
+    sliding_window_global_every: int = 0
+
+    def is_local_layer(self, i: int) -> bool:
+        if self.sliding_window <= 0:
+            return False
+        g = self.sliding_window_global_every
+        return g <= 0 or (i + 1) % g != 0
 
     @property
     def q_size(self) -> int:

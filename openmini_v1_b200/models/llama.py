@@ -176,6 +176,7 @@ class DecoderLM(nn.Module):
 
     def _use_sp(self, T: int) -> bool:
         return (self._sp is not None and self._sp.fits(T) and not self.cfg.dsa.enabled
+                and self.cfg.sliding_window <= 0
                 and not any("router" in L for L in self.layers))
 
     def _tp_sum(self, t):
@@ -247,6 +248,9 @@ class DecoderLM(nn.Module):
         if cfg.dsa.enabled:
             from .dsa import dsa_attention
             attn = dsa_attention(self, i, L, a, qkv, fb, kv)
+        elif cfg.is_local_layer(i):
+            from .window import window_attention
+            attn = window_attention(self, qkv, kv.k[i], kv.v[i], fb, cfg.sliding_window)
         elif fb.prefill_tiles is not None and self.hd == 128:
             attn = ops.flash_prefill(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
                                      fb.prefill_tiles, self.hq, self.scale)

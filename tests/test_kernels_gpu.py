@@ -413,3 +413,22 @@ def test_flash_prefill_lse_and_ring_merge():
             o_s, l_s = attend(q[sl], k[s * C:(s + 1) * C], v[s * C:(s + 1) * C], sc, causal=False)
             out, lse = merge(out, lse, o_s, l_s)
         _close(out.cpu(), want[sl])
+
+
+def test_sliding_window_attention_gpu():
+    """Window attention (device index lists + sparse-gather kernel) against the CPU path."""
+    from types import SimpleNamespace
+    from openmini_v1_b200.models.window import window_attention
+    Hq, Hkv, D, W = 8, 2, 128, 64
+    lens = [1, 40, 300, 700]
+    S = len(lens)
+    kc, vc, bt = _paged_setup(S, Hkv, D, lens, 80, seed=500)
+    q = _rand(S, Hq * D, seed=501)
+    fb = SimpleNamespace(max_ctx=max(lens), block_tables=bt, row_seq=torch.arange(S, dtype=torch.int32, device=DEV),
+                         row_ctx=torch.tensor(lens, dtype=torch.int32, device=DEV), prefill_tiles=None)
+    m = SimpleNamespace(hq=Hq, hd=D, scale=1 / math.sqrt(D))
+    out = window_attention(m, q, kc, vc, fb, W)
+    ops.check_status()
+    fbc = SimpleNamespace(max_ctx=fb.max_ctx, block_tables=bt.cpu(), row_seq=fb.row_seq.cpu(), row_ctx=fb.row_ctx.cpu(),
+                          prefill_tiles=None)
+    _close(out.cpu(), window_attention(m, q.cpu(), kc.cpu(), vc.cpu(), fbc, W))
