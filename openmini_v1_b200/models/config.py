@@ -64,6 +64,8 @@ class ModelConfig:
     # layer i is local unless (i + 1) % sliding_window_global_every == 0 (0: every layer local)
     sliding_window: int = 0
     sliding_window_global_every: int = 0
+    # streaming attention (attention sinks): local layers also keep the first N positions
+    attention_sinks: int = 0
 
     def is_local_layer(self, i: int) -> bool:
         if self.sliding_window <= 0:

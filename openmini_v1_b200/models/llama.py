@@ -250,7 +250,7 @@ class DecoderLM(nn.Module):
             attn = dsa_attention(self, i, L, a, qkv, fb, kv)
         elif cfg.is_local_layer(i):
             from .window import window_attention
-            attn = window_attention(self, qkv, kv.k[i], kv.v[i], fb, cfg.sliding_window)
+            attn = window_attention(self, qkv, kv.k[i], kv.v[i], fb, cfg.sliding_window, cfg.attention_sinks)
         elif fb.prefill_tiles is not None and self.hd == 128:
             attn = ops.flash_prefill(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
                                      fb.prefill_tiles, self.hq, self.scale)

@@ -61,3 +61,15 @@ def test_window_model_prefill_equals_decode():
     ra = LLMEngine(a, EngineConfig(max_num_seqs=2, max_model_len=128)).generate([prompt], sp)[0]
     rb = LLMEngine(b, EngineConfig(max_num_seqs=2, max_model_len=128)).generate([prompt], sp)[0]
     assert ra.output_token_ids == rb.output_token_ids
+
+
+def test_attention_sinks_indices():
+    sel, n = window_indices(torch.tensor([1, 3, 5, 9, 20], dtype=torch.int32), 4, 2)
+    got = [r[:k] for r, k in zip(sel.tolist(), n.tolist())]
+    assert got == [[0], [0, 1, 2], [0, 1, 2, 3, 4], [0, 1, 5, 6, 7, 8], [0, 1, 16, 17, 18, 19]]
+    cfg = tiny()
+    cfg.sliding_window, cfg.attention_sinks = 6, 2
+    m = DecoderLM(cfg, device="cpu", seed=5)
+    r = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=128)).generate(
+        [list(range(10, 40))], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
+    assert len(r.output_token_ids) == 3
