@@ -50,6 +50,8 @@ class ForwardBatch:
     record_routing: dict | None = None
     # prefill query tiles [n, 4] int32 (row_start, rows, seq, keys of the last row) or None
     prefill_tiles: torch.Tensor | None = None
+    # multimodal input: (rows int64 [n], embeddings [n, D]) that replace the token embeddings
+    embed_override: tuple | None = None
 
 
 @dataclass
@@ -190,9 +192,12 @@ class DecoderLM(nn.Module):
 
     def forward(self, fb: ForwardBatch, kv: KVCache) -> torch.Tensor:
         """Returns final-normed hidden states of rows ``fb.logits_idx``: [S', D]."""
-        if self.par.tp > 1 and self._use_sp(fb.input_ids.shape[0]):
+        if self.par.tp > 1 and self._use_sp(fb.input_ids.shape[0]) and fb.embed_override is None:
             return self.forward_sp(fb, kv)
         h = self.embed_tokens(fb.input_ids)  # residual stream [T, D]
+        if fb.embed_override is not None:  # image features in place of placeholder tokens
+            rows, emb = fb.embed_override
+            h.index_copy_(0, rows.to(h.device), emb.to(h.dtype))
         delta = None
         for i, L in enumerate(self.layers):
             h, delta = self.layer_forward(i, L, h, delta, fb, kv)

@@ -432,3 +432,18 @@ def test_sliding_window_attention_gpu():
     fbc = SimpleNamespace(max_ctx=fb.max_ctx, block_tables=bt.cpu(), row_seq=fb.row_seq.cpu(), row_ctx=fb.row_ctx.cpu(),
                           prefill_tiles=None)
     _close(out.cpu(), window_attention(m, q.cpu(), kc.cpu(), vc.cpu(), fbc, W))
+
+
+def test_vision_encoder_gpu():
+    """ViT encoder on the GPU kernels (GEMM, LayerNorm, GELU, bidirectional FlashAttention)
+    against the same encoder's fp32 CPU statement."""
+    from openmini_v1_b200.models.vision import VisionConfig, VisionEncoder, preprocess
+    cfg = VisionConfig(image_size=224, patch_size=16, hidden_size=1024, num_layers=2, num_heads=8, mlp_size=2048,
+                       lm_hidden=512)
+    enc = VisionEncoder(cfg, device=DEV, seed=2)
+    cpu = VisionEncoder(cfg, device="cpu", seed=2)
+    img = torch.rand(224, 224, 3, generator=torch.Generator().manual_seed(3))
+    p = preprocess(img, cfg)[0]
+    got = enc.encode(p)
+    ops.check_status()
+    _close(got.cpu(), cpu.encode(p), rtol=5e-2, atol=5e-2)
