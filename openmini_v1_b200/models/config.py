@@ -18,7 +18,8 @@ class MoEConfig:
     num_experts: int = 0           # 0 = dense FFN everywhere
     top_k: int = 2
     expert_ffn: int = 0
-    num_shared_experts: int = 0
+    num_shared_experts: int = 0    # always-on SwiGLU experts added to the routed output
+    num_zero_experts: int = 0      # zero-computation experts (output = input), LongCat-style
     layer_rule: str = "all"        # "all" | "cyclic" (layer % period == period - 1)
     cycle_period: int = 3
     ffn_prefix_layers: int = 0     # first N layers stay dense

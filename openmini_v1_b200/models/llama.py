@@ -125,9 +125,14 @@ class DecoderLM(nn.Module):
             }
             if cfg.moe.is_moe_layer(i):
                 E, Fe = cfg.moe.num_experts, cfg.moe.expert_ffn
-                L["router"] = self._randn(shared, E, D, std=std)
+                L["router"] = self._randn(shared, E + cfg.moe.num_zero_experts, D, std=std)
                 L["experts_gate_up"] = [self._randn(gen, 2 * Fe, D, std=std) for _ in range(E)]
                 L["experts_down"] = [self._randn(gen, D, Fe, std=std) for _ in range(E)]
+                ns = cfg.moe.num_shared_experts
+                if ns:  # shared experts as one SwiGLU FFN of width ns * Fe (column-parallel under TP)
+                    Fs = _shard(ns * Fe, self.par.tp, "shared expert width")
+                    L["shared_gate_up"] = self._randn(gen, 2 * Fs, D, std=std)
+                    L["shared_down"] = self._randn(gen, D, Fs, std=std)
             else:
                 L["gate_up"] = self._randn(gen, 2 * self.ffn, D, std=std)
                 L["down"] = self._randn(gen, D, self.ffn, std=std)

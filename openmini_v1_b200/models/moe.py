@@ -72,13 +72,32 @@ def moe_forward_device(model, layer_idx, L, x, fb):
     return out
 
 
+def load_balance_loss(router_logits: torch.Tensor, ids: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """Switch-style auxiliary loss E * sum_e f_e * P_e: f_e the fraction of (token, choice)
+    pairs routed to expert e, P_e the mean router probability of e (reference: MoE v2
+    load-balance loss, openmini-server/src/model/inference/gguf.rs:1298)."""
+    probs = torch.softmax(router_logits.float(), -1)[:, :num_experts]
+    f = torch.bincount(ids.reshape(-1).clamp(max=num_experts), minlength=num_experts + 1)[:num_experts].float()
+    f = f / max(1, ids.numel())
+    return num_experts * (f * probs.mean(0)).sum()
+
+
 def moe_forward(model, layer_idx, L, x, fb):
+    """Routed experts (+ zero-computation experts) + shared experts."""
+    y = _routed(model, layer_idx, L, x, fb)
+    if "shared_gate_up" in L:
+        y = y + ops.linear(ops.silu_mul(ops.linear(x, L["shared_gate_up"])), L["shared_down"])
+    return y
+
+
+def _routed(model, layer_idx, L, x, fb):
     cfg = model.cfg.moe
     T, D = x.shape
     ep = getattr(model, "_ep", None)
     if ep is not None and ep.size > 1:  # expert parallel: all-to-all dispatch / combine
         return ep.forward(model, layer_idx, L, x, fb)
-    if (x.is_cuda and isinstance(L["experts_gate_up"][0], torch.Tensor) and x.dtype == torch.bfloat16
+    if (x.is_cuda and cfg.num_zero_experts == 0 and isinstance(L["experts_gate_up"][0], torch.Tensor)
+            and x.dtype == torch.bfloat16
             and D % 64 == 0 and cfg.expert_ffn % 64 == 0 and cfg.num_experts <= 256 and cfg.top_k <= 8):
         return moe_forward_device(model, layer_idx, L, x, fb)
     logits = ops.linear(x, L["router"])
@@ -91,14 +110,18 @@ def moe_forward(model, layer_idx, L, x, fb):
     tok = torch.arange(T, device=x.device).repeat_interleave(cfg.top_k)
     wt = w.reshape(-1)
     order = torch.argsort(flat, stable=True)
-    counts = torch.bincount(flat, minlength=cfg.num_experts).tolist()
+    counts = torch.bincount(flat, minlength=cfg.num_experts + cfg.num_zero_experts).tolist()
     start = 0
+    E = cfg.num_experts
     for e, n in enumerate(counts):
         if n == 0:
             continue
         sel = order[start:start + n]
         start += n
         t_idx = tok[sel]
+        if e >= E:  # zero-computation expert: passes its tokens through, weighted
+            out.index_add_(0, t_idx, x.index_select(0, t_idx).float() * wt[sel, None])
+            continue
         xe = x.index_select(0, t_idx)
         gu = ops.linear(xe, L["experts_gate_up"][e])
         y = ops.linear(ops.silu_mul(gu), L["experts_down"][e])

@@ -60,6 +60,8 @@ class ExpertParallel:
         T, D = x.shape
         k, E, W = cfg.top_k, cfg.num_experts, self.size
         n_local = E // W
+        if cfg.num_zero_experts:
+            raise NotImplementedError("zero-computation experts are routed locally; use ep=1 for such layers")
         logits = ops.linear(x, L["router"])
         forced = fb.forced_routing.get(layer_idx) if fb is not None and fb.forced_routing else None
         ids, w = route(logits, k, forced)
