@@ -47,6 +47,7 @@ class EngineConfig:
     eos_token_id: int | None = None
     seed: int = 0
     speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
+    draft_engine: object = None            # with speculative_k: an LLMEngine of a draft model proposes instead
     preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)
 
 
@@ -103,8 +104,9 @@ class LLMEngine:
         self.graphs = None
         self.spec = None
         if self.cfg.speculative_k > 0:
-            from .speculative import NgramProposer
-            self.spec = NgramProposer(self.cfg.speculative_k)
+            from .speculative import DraftModelProposer, NgramProposer
+            self.spec = (DraftModelProposer(self.cfg.draft_engine, self.cfg.speculative_k)
+                         if self.cfg.draft_engine is not None else NgramProposer(self.cfg.speculative_k))
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "preemptions": 0}
         if self.is_cuda and self.cfg.use_cuda_graph:
             from .cuda_graph import DecodeGraphs

@@ -46,6 +46,25 @@ class NgramProposer:
         return []
 
 
+class DraftModelProposer:
+    """Draft-model proposer (the reference's draft / verify scheme): a smaller model of the
+    same vocabulary runs greedily for k tokens from the sequence so far. It serves from
+    its own engine with the prefix cache on, so consecutive proposals for one sequence
+    re-use the draft KV of the shared prefix and cost about k draft decode steps."""
+
+    def __init__(self, draft_engine, k: int = 4):
+        from .request import SamplingParams
+        self.eng, self.k = draft_engine, k
+        self._sp = SamplingParams
+
+    def propose(self, toks, k: int | None = None) -> list:
+        k = self.k if k is None else k
+        if k <= 0:
+            return []
+        r = self.eng.generate([list(toks)], self._sp(temperature=0.0, max_tokens=k, ignore_eos=True))[0]
+        return list(r.output_token_ids)
+
+
 def eligible(r) -> bool:
     p = r.params
     return (p.temperature == 0.0 and p.repetition_penalty == 1.0 and not p.logprobs and not p.return_sampling_mask

@@ -100,6 +100,16 @@ def test_speculative_ngram_matches_greedy():
     spec = e.generate([pat, pat[:13]], sp)
     assert [r.output_token_ids for r in spec] == [r.output_token_ids for r in base]
     assert e.stats["spec_proposed"] > 0
+    # draft-model proposer: the model itself as its own draft accepts every proposal
+    draft = LLMEngine(m, EngineConfig(max_num_seqs=1, max_model_len=256))
+    e2 = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256, speculative_k=3, draft_engine=draft))
+    spec2 = e2.generate([pat, pat[:13]], sp)
+    assert [r.output_token_ids for r in spec2] == [r.output_token_ids for r in base]
+    assert e2.stats["spec_accepted"] >= e2.stats["spec_proposed"] - 4  # drafts cut at max_tokens only
+    # a different (weaker) draft model still yields exactly the greedy output
+    other = LLMEngine(DecoderLM(tiny(), device="cpu", seed=9), EngineConfig(max_num_seqs=1, max_model_len=256))
+    e3 = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256, speculative_k=3, draft_engine=other))
+    assert [r.output_token_ids for r in e3.generate([pat, pat[:13]], sp)] == [r.output_token_ids for r in base]
 
 
 def test_swap_preemption_and_session_persistence(tmp_path):
