@@ -7,7 +7,8 @@ void om_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<
 std::vector<int64_t> om_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, bool allow_split);
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
-                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer);
+                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer,
+                c10::optional<torch::Tensor> sem);
 void om_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w, torch::Tensor out,
                 double eps);
 void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, torch::Tensor out,
@@ -80,7 +81,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wq", &om_gemm_wq, "weight-only quantised tcgen05 GEMM (0 = Q4 block-32, 1 = INT8 per row)",
         py::arg("x"), py::arg("qtiles"), py::arg("scales"), py::arg("qtype"), py::arg("out"),
         py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
-        py::arg("force_swap") = -1, py::arg("force_splits") = 0, py::arg("peer") = std::vector<int64_t>{});
+        py::arg("force_swap") = -1, py::arg("force_splits") = 0, py::arg("peer") = std::vector<int64_t>{},
+        py::arg("sem") = py::none());
   m.def("rmsnorm", &om_rmsnorm, py::arg("x"), py::arg("delta"), py::arg("w"), py::arg("out"), py::arg("eps"));
   m.def("layernorm", &om_layernorm);
   m.def("silu_mul", &om_silu_mul);

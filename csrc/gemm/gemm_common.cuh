@@ -68,13 +68,21 @@ struct GemmArgs {
   int rgroup;        // weight-only SWAP: weight row-tiles per unit (tiles_r counts groups)
   int wt_tiles;      // weight-only: number of 128-row weight tiles
   int chunk;         // weight-only: K blocks per copy chunk (divides num_kb and kb_per_split)
+  // In-kernel split-K reduction (weight-only GEMM): with sem != nullptr the CTA that
+  // finishes the last split of a tile sums the fp32 partials and applies the final
+  // epilogue (yepi into yout / peers, + yresid) itself; sem[tile] counts finished splits
+  // and is reset by that CTA, so the buffer must start zeroed.
+  int* sem;
+  int yepi;
+  void* yout;
+  const __nv_bfloat16* yresid;
   PeerOut po;        // peer output (po.pworld > 0), see PeerOut
 };
 
 // Row pointer of output row m (local Y, or the owner's slot in peer mode).
-__device__ __forceinline__ __nv_bfloat16* out_row(const GemmArgs& g, int m) {
+__device__ __forceinline__ __nv_bfloat16* out_row(const GemmArgs& g, void* out, int m) {
   if (g.po.pworld > 0) return peer_row(g.po, g.ldo, m);
-  return reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ldo;
+  return reinterpret_cast<__nv_bfloat16*>(out) + (size_t)m * g.ldo;
 }
 
 __device__ __forceinline__ void unit_coords(const GemmArgs& g, int u, int& tr, int& tc, int& sp) {
@@ -92,13 +100,13 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& g, int u, int& tr, i
 }
 
 // Thread owns accumulator row r (global MMA row), columns c0 .. c0+31.
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&v)[32], int r, int c0, int sp) {
+// One thread's 32 accumulator columns f of row r -> output, with the epilogue kind,
+// output and residual given explicitly (the split-K finisher passes the final ones).
+__device__ __forceinline__ void epilogue_f(const GemmArgs& g, float (&f)[32], int r, int c0, int sp, int epi,
+                                           void* outp, const __nv_bfloat16* resid) {
   if (r >= g.rows || c0 >= g.cols) return;
   const int ncol = min(32, g.cols - c0);
-  float f[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-  if (g.wscale && g.epi != EPI_PARTIAL) {
+  if (g.wscale && epi != EPI_PARTIAL) {
     if (g.swap) {
       const float s = g.wscale[r];
 #pragma unroll
@@ -109,8 +117,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
         if (j < ncol) f[j] *= g.wscale[c0 + j];
     }
   }
-  if (g.epi == EPI_PARTIAL) {
-    float* P = reinterpret_cast<float*>(g.out);
+  if (epi == EPI_PARTIAL) {
+    float* P = reinterpret_cast<float*>(outp);
     if (!g.swap) {
       float* dst = P + ((size_t)sp * g.rows + r) * g.cols + c0;
       if (ncol == 32 && (g.cols & 3) == 0) {
@@ -130,15 +138,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
     return;
   }
   if (!g.swap) {
-    __nv_bfloat16* dst = out_row(g, r) + c0;
-    const __nv_bfloat16* rs = g.resid ? g.resid + (size_t)r * g.ldo + c0 : nullptr;
+    __nv_bfloat16* dst = out_row(g, outp, r) + c0;
+    const __nv_bfloat16* rs = resid ? resid + (size_t)r * g.ldo + c0 : nullptr;
     if (ncol == 32 && (g.ldo & 7) == 0) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
         float t[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) t[q] = f[j + q];
-        if (g.epi == EPI_RESID) {
+        if (epi == EPI_RESID) {
           const uint4 rv = *reinterpret_cast<const uint4*>(rs + j);
           t[0] += bf16lo(rv.x); t[1] += bf16hi(rv.x); t[2] += bf16lo(rv.y); t[3] += bf16hi(rv.y);
           t[4] += bf16lo(rv.z); t[5] += bf16hi(rv.z); t[6] += bf16lo(rv.w); t[7] += bf16hi(rv.w);
@@ -153,7 +161,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
       for (int j = 0; j < 32; ++j) {
         if (j < ncol) {
           float t = f[j];
-          if (g.epi == EPI_RESID) t += __bfloat162float(rs[j]);
+          if (epi == EPI_RESID) t += __bfloat162float(rs[j]);
           dst[j] = __float2bfloat16_rn(t);
         }
       }
@@ -163,11 +171,42 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
     for (int j = 0; j < 32; ++j) {
       if (j < ncol) {
         float t = f[j];
-        if (g.epi == EPI_RESID) t += __bfloat162float(g.resid[(size_t)(c0 + j) * g.ldo + r]);
-        out_row(g, c0 + j)[r] = __float2bfloat16_rn(t);
+        if (epi == EPI_RESID) t += __bfloat162float(resid[(size_t)(c0 + j) * g.ldo + r]);
+        out_row(g, outp, c0 + j)[r] = __float2bfloat16_rn(t);
       }
     }
   }
+}
+
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&v)[32], int r, int c0, int sp) {
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+  epilogue_f(g, f, r, c0, sp, g.epi, g.out, g.resid);
+}
+
+// Split-K finisher for the thread's 32 columns of row r: sum the fp32 partial planes
+// of every split (L2 loads: the other splits were written by other CTAs) and apply the
+// final epilogue.
+__device__ __forceinline__ void splitk_finish_chunk(const GemmArgs& g, int r, int c0) {
+  if (r >= g.rows || c0 >= g.cols) return;
+  const int ncol = min(32, g.cols - c0);
+  const float* P = reinterpret_cast<const float*>(g.out);
+  const size_t plane = (size_t)g.rows * g.cols;
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = 0.f;
+  for (int s = 0; s < g.splits; ++s) {
+    const float* base = P + s * plane;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < ncol) {
+        const size_t o = g.swap ? (size_t)(c0 + j) * g.rows + r : (size_t)r * g.cols + c0 + j;
+        f[j] += __ldcg(base + o);
+      }
+    }
+  }
+  epilogue_f(g, f, r, c0, 0, g.yepi, g.yout, g.yresid);
 }
 
 }  // namespace om

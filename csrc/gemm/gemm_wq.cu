@@ -41,7 +41,8 @@ static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g
 // scales: INT8 only, fp32 [N] per-row scale (applied in the epilogue).
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
-                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer) {
+                torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer,
+                c10::optional<torch::Tensor> sem) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_wq: x");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.dim() == 2, "gemm_wq: out");
   const int M = x.size(0), K = x.size(1), N = out.size(1);
@@ -142,10 +143,19 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
   const __nv_bfloat16* rp = resid.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
   if (resid.has_value())
     TORCH_CHECK(resid->sizes() == out.sizes() && resid->stride(0) == out.stride(0), "gemm_wq: resid layout");
+  const bool fused_reduce = splits > 1 && sem.has_value() && sem->numel() >= (int64_t)g.tiles_r * g.tiles_c;
   if (splits > 1) {
     g.epi = om::EPI_PARTIAL;
     g.out = ws;
     g.resid = nullptr;
+    if (fused_reduce) {  // the last split of each tile finishes it inside the GEMM kernel
+      TORCH_CHECK(sem->scalar_type() == at::kInt && sem->is_contiguous(), "gemm_wq: sem must be zeroed int32");
+      g.sem = sem->data_ptr<int>();
+      g.yepi = rp ? om::EPI_RESID : om::EPI_STORE;
+      g.yout = out.data_ptr();
+      g.yresid = rp;
+      if (has_peer) g.po = po;
+    }
   } else {
     g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
     g.out = out.data_ptr();
@@ -162,7 +172,7 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     om::dispatch<om::WQ_Q4>(bx, swap, tx, g, grid, st);
   else
     om::dispatch<om::WQ_I8>(bx, swap, tx, g, grid, st);
-  if (splits > 1)
+  if (splits > 1 && !fused_reduce)
     om::launch_splitk_reduce(ws, splits, M, N, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rp,
                              qtype == 1 ? scales->data_ptr<float>() : nullptr, st, has_peer ? &po : nullptr);
 }

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* tfull = raw_empty + RD;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ int s_last;            // split-K finisher flag of the current unit (epilogue warps)
+  __shared__ uint64_t fin_bar[2];   // epilogue-warp rendezvous of the finisher (bounded waits)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(512, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
+      mbar_init(&fin_bar[a], 128);
     }
     fence_barrier_init();
   }
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(512, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    int local = 0;
+    int local = 0, nfin = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
       int tr, tc, sp;
       unit_coords(g, u, tr, tc, sp);
@@ -398,6 +401,31 @@ __global__ void __launch_bounds__(512, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (g.sem != nullptr && g.splits > 1) {
+        // in-kernel split-K reduction: the CTA that completes a tile's last split finishes it
+        __threadfence();  // this thread's partial stores, visible device-wide
+        mbar_arrive(&fin_bar[0]);
+        if (!mbar_wait(&fin_bar[0], nfin & 1, g.status, OM_ERR_WAIT_ACCUM)) break;
+        if (q == 0 && lane == 0) {
+          const int tile = tr * g.tiles_c + tc;
+          const int prev = atomicAdd(&g.sem[tile], 1);
+          s_last = prev == g.splits - 1;
+          if (s_last) g.sem[tile] = 0;  // ready for the next launch
+        }
+        mbar_arrive(&fin_bar[1]);
+        if (!mbar_wait(&fin_bar[1], nfin & 1, g.status, OM_ERR_WAIT_ACCUM)) break;
+        ++nfin;
+        if (s_last) {
+          __threadfence();
+          const int nRf = unit_rows(g, tr);
+          for (int j = 0; j < nRf; ++j) {
+            const int wt = SWAP ? tr * g.rgroup + j : tr;
+            const int r = wt * 128 + q * 32 + lane;
+#pragma unroll 1
+            for (int cc = 0; cc < BN_MMA / 32; ++cc) splitk_finish_chunk(g, r, tc * BN_MMA + cc * 32);
+          }
+        }
+      }
     }
   }
 

@@ -32,6 +32,17 @@ class DeviceContext:
         self._ws = {}
         self.frozen = False  # set while capturing a CUDA graph: no reallocation allowed
 
+    def semaphores(self) -> torch.Tensor:
+        """Zeroed int32 tile counters of the in-kernel split-K reduction (every kernel that
+        uses them leaves them zeroed again)."""
+        s = self._ws.get("__sem")
+        if s is None:
+            if self.frozen:
+                raise RuntimeError("semaphores first requested during graph capture")
+            s = torch.zeros(1 << 16, dtype=torch.int32, device=self.device)
+            self._ws["__sem"] = s
+        return s
+
     def workspace(self, name: str, numel: int) -> torch.Tensor:
         buf = self._ws.get(name)
         if buf is None or buf.numel() < numel:

@@ -447,3 +447,27 @@ def test_vision_encoder_gpu():
     got = enc.encode(p)
     ops.check_status()
     _close(got.cpu(), cpu.encode(p), rtol=5e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("kind,M", [("q4", 7), ("q4", 200), ("int8", 33)])
+def test_gemm_wq_fused_splitk(kind, M):
+    """In-kernel split-K reduction (last split of a tile finishes it) equals the separate
+    reduction kernel, on repeated launches (the tile counters reset themselves)."""
+    N, K = 1536, 2048
+    x = _rand(M, K, seed=600)
+    w = _rand(N, K, std=0.05, seed=601)
+    r = _rand(M, N, seed=602)
+    wt = Q4Weight.from_dense(w) if kind == "q4" else Int8Weight.from_dense(w)
+    sc = None if kind == "q4" else wt.scale
+    c = ops.ctx(DEV)
+    ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
+    sem = c.semaphores()
+    want = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    _native.C().gemm_wq(x, wt.tiles, sc, wt.qtype, want, r, ws, c.status, force_splits=4)
+    for _ in range(3):
+        got = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        _native.C().gemm_wq(x, wt.tiles, sc, wt.qtype, got, r, ws, c.status, force_splits=4, sem=sem)
+        torch.cuda.synchronize()
+        ops.check_status()
+        torch.testing.assert_close(got.float(), want.float(), rtol=1e-2, atol=1e-2)
+    assert int(sem.abs().sum()) == 0
