@@ -15,6 +15,8 @@ on the CPU. Reference formats: openmini-server/src/model/inference/quant.rs:56-4
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .. import _native, ops
@@ -172,6 +174,9 @@ class Int8Weight:
         return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid, peer)
 
 
+_FUSED_SPLITK = os.environ.get("OM_WQ_FUSED_SPLITK", "0") == "1"
+
+
 def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
@@ -181,12 +186,12 @@ def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     c = ops.ctx(x.device)
     ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    # The in-kernel split-K finisher (``sem=ops.ctx(dev).semaphores()``) is correct but measured
-    # 3x slower end to end on the 70B decode step, so the separate reduction kernel stays.
+    # The in-kernel split-K finisher (``sem``) is correct but measured ~3.7x slower on the
+    # decode GEMMs, so the separate reduction kernel stays unless OM_WQ_FUSED_SPLITK=1.
+    kw = {"sem": c.semaphores()} if _FUSED_SPLITK else {}
     if peer is not None:
-        _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status, peer=peer)
-    else:
-        _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status)
+        kw["peer"] = peer
+    _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status, **kw)
     return out
 
 
