@@ -23,7 +23,10 @@ class _Linear(torch.autograd.Function):
         gy = gy.contiguous().to(x.dtype)
         gx = gw = None
         if ctx.needs_input_grad[0]:
-            gx = ops.linear(gy, w.t().contiguous())                       # [M, K] = dY @ W
+            padn = (-gy.shape[1]) % 8  # the output dim becomes the reduction dim (e.g. a 4-expert router)
+            g2 = torch.nn.functional.pad(gy, (0, padn)) if padn else gy
+            wt = torch.nn.functional.pad(w.t(), (0, padn)) if padn else w.t()
+            gx = ops.linear(g2, wt.contiguous())                          # [M, K] = dY @ W
         if ctx.needs_input_grad[1]:
             pad = (-x.shape[0]) % 8  # the token dim becomes the reduction dim: keep rows 16-byte aligned
             xp = torch.nn.functional.pad(x, (0, 0, 0, pad)) if pad else x
