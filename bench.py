@@ -32,7 +32,7 @@ import threading
 import time
 
 METRIC = "decode tok/s + p50 TTFT/TPOT, 70B-shape TP=8, at 1/2/4/8 B200 (device, max/rank)"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this model/config
+BASELINE_VALUE = None  # the reference publishes no number for this model/config
 
 
 def _args():
@@ -137,7 +137,7 @@ def main():
     from openmini_v1_b200.engine.request import SamplingParams
     from openmini_v1_b200.models.config import preset
     from openmini_v1_b200.models.llama import DecoderLM
-    from openmini_v1_b200.parallel.fused import make_tp_comm
+    from openmini_v1_b200.parallel.fused import attach_tp_transport
     from openmini_v1_b200.parallel.state import ParallelState, init_distributed
 
     rank, world = init_distributed()
@@ -154,11 +154,7 @@ def main():
     max_len = a.prompt_max + a.out_tokens
     t_init = time.monotonic()
     model = DecoderLM(cfg, par=par, device=dev, seed=a.seed, weight_format=a.quant)
-    if world > 1:
-        model.set_comm(make_tp_comm(par, dev))
-        if a.tp_transport == "symm":
-            from openmini_v1_b200.parallel.symm import make_sp
-            model.set_sp(make_sp(par, dev, max_rows=4096, dim=cfg.hidden_size))
+    attach_tp_transport(model, par, dev, a.tp_transport, max_rows=4096)
     torch.cuda.synchronize()
     init_s = time.monotonic() - t_init
     eng = LLMEngine(model, EngineConfig(max_num_seqs=B, max_num_batched_tokens=16384, max_model_len=max_len,

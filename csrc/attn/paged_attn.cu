@@ -30,7 +30,8 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnArgs a) {
   __shared__ float m_s[G], l_s[G];
 
   const int row = blockIdx.x, kvh = blockIdx.y, part = blockIdx.z;
-  const int ctx = a.row_ctx[row];
+  int seq;
+  const int ctx = checked_ctx(a, row, seq);
   const int start = part * ATT_PART;
   const int tid = threadIdx.x;
   const size_t pbase = ((size_t)row * a.Hq + (size_t)kvh * G) * a.NP + part;
@@ -43,7 +44,6 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnArgs a) {
     return;
   }
   const int end = min(ctx, start + ATT_PART);
-  const int seq = a.row_seq[row];
   const int* bt = a.block_tables + (size_t)seq * a.max_blocks;
 
   for (int i = tid; i < G * D; i += NT) {
@@ -192,6 +192,7 @@ void om_paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   a.vc = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
   a.block_tables = block_tables.data_ptr<int>();
   a.max_blocks = block_tables.size(1);
+  a.num_seqs = block_tables.size(0);
   a.row_seq = row_seq.data_ptr<int>();
   a.row_ctx = row_ctx.data_ptr<int>();
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -233,6 +234,8 @@ int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_
 //
 // Limits and behaviour:
 //   * The scratch array holds OM_NOALLOC_SCRATCH_FLOATS fp32 values (16 MiB).
+//   * Rows whose sequence index or context exceeds the block table or max_ctx
+//     set OM_ERR_BOUNDS (5) in *status and are clamped; the call still returns 0.
 //     A call needs rows * Hq * ceil(max_ctx / 512) * (head_dim + 2) floats and
 //     is rejected with OM_NOALLOC_TOO_LARGE if that exceeds the array.
 //   * Every GPU that loads this library reserves the 16 MiB until the process
@@ -247,17 +250,9 @@ int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_
 //   * No cudaMalloc / cudaFree or allocating library routine is called.
 // ============================================================================
 #include <mutex>
-
-#define OM_NOALLOC_SCRATCH_FLOATS (4u << 20)
+#include "../../include/openmini_b200.h"
 
 static __device__ __align__(256) float om_noalloc_scratch[OM_NOALLOC_SCRATCH_FLOATS];
-
-enum : int {
-  OM_NOALLOC_OK = 0,
-  OM_NOALLOC_TOO_LARGE = 1,   // request exceeds the fixed scratch array
-  OM_NOALLOC_BAD_ARGS = 2,    // unsupported head_dim / GQA group / null pointer
-  OM_NOALLOC_CUDA_ERROR = 3,  // symbol lookup or kernel launch failed
-};
 
 static float* om_noalloc_scratch_ptr() {
   static std::mutex mu;
@@ -273,23 +268,23 @@ static float* om_noalloc_scratch_ptr() {
   return ptrs[dev];
 }
 
-// q [rows, Hq, D] bf16 (row stride q_ld elements), caches [num_blocks, Hkv, 16, D]
-// bf16, block_tables [S, max_blocks] int32, row_seq / row_ctx [rows] int32,
-// out [rows, Hq, D] bf16 (row stride out_ld). status may be null.
-// Returns an OM_NOALLOC_* code.
+// Declared in include/openmini_b200.h (arguments and return codes documented there).
 extern "C" int om_paged_attention_noalloc(const void* q, int q_ld, const void* k_cache, const void* v_cache,
                                           int num_blocks, int Hkv, int head_dim, const int* block_tables,
-                                          int max_blocks, const int* row_seq, const int* row_ctx, int rows,
-                                          void* out, int out_ld, int Hq, int max_ctx, float scale, int* status,
-                                          cudaStream_t stream) {
+                                          int num_seqs, int max_blocks, const int* row_seq, const int* row_ctx,
+                                          int rows, void* out, int out_ld, int Hq, int max_ctx, float scale,
+                                          int* status, cudaStream_t stream) {
   if (rows <= 0) return OM_NOALLOC_OK;
   if (!q || !k_cache || !v_cache || !block_tables || !row_seq || !row_ctx || !out) return OM_NOALLOC_BAD_ARGS;
-  if (Hkv <= 0 || Hq % Hkv != 0 || (head_dim != 64 && head_dim != 128) || max_ctx <= 0) return OM_NOALLOC_BAD_ARGS;
+  if (Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0 || (head_dim != 64 && head_dim != 128) || max_ctx <= 0 ||
+      num_seqs <= 0 || max_blocks <= 0 || num_blocks <= 0)
+    return OM_NOALLOC_BAD_ARGS;
   const int G = Hq / Hkv;
   if (G != 1 && G != 2 && G != 4 && G != 5 && G != 8 && G != 16) return OM_NOALLOC_BAD_ARGS;
-  const size_t np = (size_t)(max_ctx + om::ATT_PART - 1) / om::ATT_PART;
-  const size_t need = (size_t)rows * Hq * np * (head_dim + 2);
-  if (need > OM_NOALLOC_SCRATCH_FLOATS) return OM_NOALLOC_TOO_LARGE;
+  // partitions in 64-bit, and the size check as a quotient so no product can wrap
+  const int64_t np = ((int64_t)max_ctx + om::ATT_PART - 1) / om::ATT_PART;
+  const uint64_t per_part = (uint64_t)rows * (uint64_t)Hq * (uint64_t)(head_dim + 2);
+  if ((uint64_t)np > OM_NOALLOC_SCRATCH_FLOATS / per_part) return OM_NOALLOC_TOO_LARGE;
   float* scratch = om_noalloc_scratch_ptr();
   if (!scratch) return OM_NOALLOC_CUDA_ERROR;
   om::AttnArgs a;
@@ -299,6 +294,7 @@ extern "C" int om_paged_attention_noalloc(const void* q, int q_ld, const void* k
   a.vc = static_cast<const __nv_bfloat16*>(v_cache);
   a.block_tables = block_tables;
   a.max_blocks = max_blocks;
+  a.num_seqs = num_seqs;
   a.row_seq = row_seq;
   a.row_ctx = row_ctx;
   a.out = static_cast<__nv_bfloat16*>(out);

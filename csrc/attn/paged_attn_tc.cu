@@ -106,11 +106,12 @@ __global__ void __launch_bounds__(256, 1)
       for (int it = blockIdx.x; it < t.items && ok; it += gridDim.x) {
         int row, kvh, part;
         item_coords(t, it, row, kvh, part);
-        const int ctx = a.row_ctx[row];
+        int seq;
+        const int ctx = checked_ctx(a, row, seq);
         const int start = part * ATT_PART;
         if (start >= ctx) continue;
         const int end = min(ctx, start + ATT_PART);
-        const int* bt = a.block_tables + (size_t)a.row_seq[row] * a.max_blocks;
+        const int* bt = a.block_tables + (size_t)seq * a.max_blocks;
         const int last_blk = (ctx - 1) >> 4;
         if (!mbar_wait(q_empty, (ic & 1) ^ 1, status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
         mbar_arrive_expect_tx(q_full, Q_BYTES);
@@ -150,7 +151,8 @@ __global__ void __launch_bounds__(256, 1)
       for (int it = blockIdx.x; it < t.items && ok; it += gridDim.x) {
         int row, kvh, part;
         item_coords(t, it, row, kvh, part);
-        const int ctx = a.row_ctx[row];
+        int seq;
+        const int ctx = checked_ctx(a, row, seq);
         const int start = part * ATT_PART;
         if (start >= ctx) continue;
         const int nch = (min(ctx, start + ATT_PART) - start + CH - 1) / CH;
@@ -208,7 +210,8 @@ __global__ void __launch_bounds__(256, 1)
     for (int it = blockIdx.x; it < t.items && ok; it += gridDim.x) {
       int row, kvh, part;
       item_coords(t, it, row, kvh, part);
-      const int ctx = a.row_ctx[row];
+      int seq;
+        const int ctx = checked_ctx(a, row, seq);
       const int start = part * ATT_PART;
       if (start >= ctx) continue;
       const int end = min(ctx, start + ATT_PART);
@@ -331,6 +334,7 @@ void om_paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
   a.vc = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
   a.block_tables = block_tables.data_ptr<int>();
   a.max_blocks = block_tables.size(1);
+  a.num_seqs = block_tables.size(0);
   a.row_seq = row_seq.data_ptr<int>();
   a.row_ctx = row_ctx.data_ptr<int>();
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());

@@ -64,19 +64,19 @@ struct GemmArgs {
   const uint8_t* wtiles;       // quantised weights, pre-tiled (weight-only GEMM)
   int ldo;           // leading dimension of Y / resid (elements)
   int* status;
-  int dbg;           // profiling knobs of the weight-only kernel (0 in production)
   int rgroup;        // weight-only SWAP: weight row-tiles per unit (tiles_r counts groups)
   int wt_tiles;      // weight-only: number of 128-row weight tiles
   int chunk;         // weight-only: K blocks per copy chunk (divides num_kb and kb_per_split)
-  // In-kernel split-K reduction (weight-only GEMM): with sem != nullptr the CTA that
-  // finishes the last split of a tile sums the fp32 partials and applies the final
-  // epilogue (yepi into yout / peers, + yresid) itself; sem[tile] counts finished splits
-  // and is reset by that CTA, so the buffer must start zeroed.
+  // Stream-K decode kernel: per-row-group counters of finished segments (zeroed
+  // before the first launch; the finishing CTA zeroes its group's counter again).
   int* sem;
-  int yepi;
-  void* yout;
-  const __nv_bfloat16* yresid;
   PeerOut po;        // peer output (po.pworld > 0), see PeerOut
+  // Stream-K decode kernel (gemm_wq_dec.cuh): the sk_total work items (row group,
+  // K chunk) are cut into gridDim.x equal contiguous ranges; sk_nc chunks per group;
+  // part = fp32 partial slots [gridDim.x][2][rgroup * 128 * cols_pad].
+  long long sk_total;
+  int sk_nc;
+  float* part;
 };
 
 // Row pointer of output row m (local Y, or the owner's slot in peer mode).
@@ -183,30 +183,6 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
   epilogue_f(g, f, r, c0, sp, g.epi, g.out, g.resid);
-}
-
-// Split-K finisher for the thread's 32 columns of row r: sum the fp32 partial planes
-// of every split (L2 loads: the other splits were written by other CTAs) and apply the
-// final epilogue.
-__device__ __forceinline__ void splitk_finish_chunk(const GemmArgs& g, int r, int c0) {
-  if (r >= g.rows || c0 >= g.cols) return;
-  const int ncol = min(32, g.cols - c0);
-  const float* P = reinterpret_cast<const float*>(g.out);
-  const size_t plane = (size_t)g.rows * g.cols;
-  float f[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) f[j] = 0.f;
-  for (int s = 0; s < g.splits; ++s) {
-    const float* base = P + s * plane;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < ncol) {
-        const size_t o = g.swap ? (size_t)(c0 + j) * g.rows + r : (size_t)r * g.cols + c0 + j;
-        f[j] += __ldcg(base + o);
-      }
-    }
-  }
-  epilogue_f(g, f, r, c0, 0, g.yepi, g.yout, g.yresid);
 }
 
 }  // namespace om

@@ -1,8 +1,8 @@
 // Host launcher of the weight-only-quantised tcgen05 GEMM (Q4 block-32 / INT8 per row).
-#include <cstdlib>
 #include "../common/om_host.h"
 #include "gemm_launch.h"
 #include "gemm_wq.cuh"
+#include "gemm_wq_dec.cuh"
 
 namespace om {
 
@@ -21,6 +21,30 @@ static void launch_wq(const CUtensorMap& tx, const GemmArgs& g, int grid, cudaSt
   OM_LAUNCH_CHECK();
 }
 
+template <int BX, int QT>
+static void launch_dec(const CUtensorMap& tx, const GemmArgs& g, int grid, cudaStream_t st) {
+  using C = WqDecCfg<BX, QT>;
+  static bool attr_set[64] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    OM_CUDA_CHECK(cudaFuncSetAttribute(gemm_wq_dec_kernel<BX, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  gemm_wq_dec_kernel<BX, QT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tx, g);
+  OM_LAUNCH_CHECK();
+}
+
+template <int QT>
+static void dispatch_dec(int bx, const CUtensorMap& tx, const GemmArgs& g, int grid, cudaStream_t st) {
+  switch (bx) {
+    case 32: return launch_dec<32, QT>(tx, g, grid, st);
+    case 64: return launch_dec<64, QT>(tx, g, grid, st);
+    default: return launch_dec<128, QT>(tx, g, grid, st);
+  }
+}
+
 template <int QT>
 static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g, int grid, cudaStream_t st) {
   if (!swap) return launch_wq<128, QT, false>(tx, g, grid, st);
@@ -37,8 +61,11 @@ static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g
 // Weight-only quantised GEMM: out[M, N] = x[M, K] @ dequant(W)^T (+ resid).
 // qtiles: uint8 [ceil(N/128), K/64, tile bytes] in the tiled device format
 //   (qtype 0, Q4: 4608-byte tiles = 128 rows x 32 B nibbles + [2][128] bf16 scales;
-//    qtype 1, INT8: 8192-byte tiles = 128 rows x 64 B);
+//    qtype 1, INT8: 8192-byte tiles = 128 rows x 64 offset-binary bytes);
 // scales: INT8 only, fp32 [N] per-row scale (applied in the epilogue).
+// Decode (M <= 128 tokens, with a workspace and the zeroed counters `sem`) runs the
+// stream-K TMEM-operand kernel (gemm_wq_dec.cuh); larger M and prefill run the
+// shared-memory-operand kernel (gemm_wq.cuh) with split-K planned by a byte model.
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
                 torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer,
@@ -72,18 +99,63 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
   g.wt_tiles = wt_tiles;
   g.tiles_c = (cols + bn_mma - 1) / bn_mma;
   g.num_kb = K / 64;
-  int splits = 1, rgroup = 1;
+  g.swap = swap ? 1 : 0;
+  g.status = status.data_ptr<int>();
+  g.ldo = out.stride(0);
+  g.wscale = qtype == 1 ? scales->data_ptr<float>() : nullptr;
+  g.wtiles = qtiles.data_ptr<uint8_t>();
   float* ws = nullptr;
   size_t ws_bytes = 0;
   if (workspace.has_value()) {
+    TORCH_CHECK(workspace->is_cuda() && workspace->scalar_type() == at::kFloat && workspace->is_contiguous(),
+                "gemm_wq: workspace must be contiguous fp32");
     ws = workspace->data_ptr<float>();
     ws_bytes = workspace->numel() * sizeof(float);
   }
-  // Plan (decode / SWAP): choose the weight row-tiles per unit R (activation reuse) and
+  const __nv_bfloat16* rp = resid.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
+  if (resid.has_value())
+    TORCH_CHECK(resid->sizes() == out.sizes() && resid->stride(0) == out.stride(0), "gemm_wq: resid layout");
+  TORCH_CHECK(x.stride(0) % 8 == 0, "gemm_wq: x row stride must be a multiple of 8 elements");
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+
+  // ---------------------------------------------------------------- stream-K decode kernel
+  const int dec_ch = qtype == 0 ? 4 : 2;
+  const int dec_r = bx == 32 ? 2 : 1;
+  if (swap && bx <= 128 && force_splits <= 0 && sem.has_value() && ws && g.num_kb % dec_ch == 0) {
+    const int groups = (wt_tiles + dec_r - 1) / dec_r;
+    const int nc = g.num_kb / dec_ch;
+    const long long total = (long long)groups * nc;
+    const int grid = (int)std::min<long long>(sms, total);
+    const size_t part_bytes = (size_t)grid * 2 * dec_r * 128 * bx * sizeof(float);
+    TORCH_CHECK(part_bytes <= ws_bytes, "gemm_wq: workspace too small for the decode partials");
+    TORCH_CHECK(sem->is_cuda() && sem->scalar_type() == at::kInt && sem->is_contiguous() && sem->numel() >= groups,
+                "gemm_wq: sem must be zeroed int32 with one counter per row group");
+    g.rgroup = dec_r;
+    g.sk_total = total;
+    g.sk_nc = nc;
+    g.part = ws;
+    g.sem = sem->data_ptr<int>();
+    g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
+    g.out = out.data_ptr();
+    g.resid = rp;
+    if (has_peer) g.po = po;
+    // activations as [K/64][M][64]: a box {64, bx, ch} is `ch` swizzled [bx][64] tiles
+    CUtensorMap tx = om::make_tmap_3d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, K / 64, x.stride(0),
+                                      64, 64, bx, dec_ch, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (qtype == 0)
+      om::dispatch_dec<om::WQ_Q4>(bx, tx, g, grid, st);
+    else
+      om::dispatch_dec<om::WQ_I8>(bx, tx, g, grid, st);
+    return;
+  }
+
+  // ---------------------------------------------------------------- shared-memory-operand kernel
+  // Plan: choose the weight row-tiles per unit R (activation reuse, decode only) and
   // the split-K factor s by a byte-count model of the busiest SM: rounds of units x
   // bytes each unit streams (R packed weight tiles + one activation tile per kb), plus
   // the fp32 partials of split-K (written and re-read, spread over the SMs).
-  const int raw_bytes = qtype == 0 ? 4608 : 8192;
+  int splits = 1, rgroup = 1;
+  const int raw_bytes = tile_bytes;
   const int x_bytes = bx * 64 * 2;
   const int rmax = swap ? std::max(1, 256 / bn_mma) : 1;
   const bool can_split = ws && N % 4 == 0;
@@ -112,17 +184,11 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
       }
     }
   }
-  static const int env_r = [] { const char* e = std::getenv("OM_WQ_R"); return e ? std::atoi(e) : 0; }();
-  static const int env_s = [] { const char* e = std::getenv("OM_WQ_S"); return e ? std::atoi(e) : 0; }();
-  static const int env_c = [] { const char* e = std::getenv("OM_WQ_CHUNK"); return e ? std::atoi(e) : 0; }();
-  if (env_r > 0) rgroup = std::min(env_r, rmax);
-  if (env_s > 0 && can_split) splits = std::min(env_s, g.num_kb);
   g.rgroup = swap ? rgroup : 1;
   g.tiles_r = swap ? (wt_tiles + g.rgroup - 1) / g.rgroup : (rows + 127) / 128;
   const int units = g.tiles_r * g.tiles_c;
   // copy chunk: the largest power of two <= the kernel's CHMAX dividing the K blocks
-  const int chmax = swap ? (bx <= 64 ? 4 : bx <= 128 ? 2 : 1) : 2;
-  int chunk = env_c > 0 ? std::min(env_c, chmax) : chmax;
+  int chunk = swap ? (bx <= 64 ? 4 : bx <= 128 ? 2 : 1) : 2;
   while (chunk > 1 && g.num_kb % chunk) chunk >>= 1;
   int kbps = (g.num_kb + splits - 1) / splits;
   kbps = (kbps + chunk - 1) / chunk * chunk;
@@ -130,49 +196,24 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
   g.chunk = chunk;
   g.splits = splits;
   g.kb_per_split = kbps;
-  g.swap = swap ? 1 : 0;
-  g.status = status.data_ptr<int>();
-  g.ldo = out.stride(0);
-  g.wscale = qtype == 1 ? scales->data_ptr<float>() : nullptr;
-  g.wtiles = qtiles.data_ptr<uint8_t>();
-  static const int dbg_env = [] {
-    const char* e = std::getenv("OM_WQ_DBG");
-    return e ? std::atoi(e) : 0;
-  }();
-  g.dbg = dbg_env;
-  const __nv_bfloat16* rp = resid.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
-  if (resid.has_value())
-    TORCH_CHECK(resid->sizes() == out.sizes() && resid->stride(0) == out.stride(0), "gemm_wq: resid layout");
-  const bool fused_reduce = splits > 1 && sem.has_value() && sem->numel() >= (int64_t)g.tiles_r * g.tiles_c;
   if (splits > 1) {
     g.epi = om::EPI_PARTIAL;
     g.out = ws;
     g.resid = nullptr;
-    if (fused_reduce) {  // the last split of each tile finishes it inside the GEMM kernel
-      TORCH_CHECK(sem->scalar_type() == at::kInt && sem->is_contiguous(), "gemm_wq: sem must be zeroed int32");
-      g.sem = sem->data_ptr<int>();
-      g.yepi = rp ? om::EPI_RESID : om::EPI_STORE;
-      g.yout = out.data_ptr();
-      g.yresid = rp;
-      if (has_peer) g.po = po;
-    }
   } else {
     g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
     g.out = out.data_ptr();
     g.resid = rp;
     if (has_peer) g.po = po;
   }
-  // activations as [K/64][M][64]: a box {64, bx, chunk} is `chunk` swizzled [bx][64] tiles
-  TORCH_CHECK(x.stride(0) % 8 == 0, "gemm_wq: x row stride must be a multiple of 8 elements");
   CUtensorMap tx = om::make_tmap_3d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, K / 64, x.stride(0), 64,
                                     64, bx, chunk, CU_TENSOR_MAP_SWIZZLE_128B);
   const int grid = std::min(units * splits, sms);
-  auto st = at::cuda::getCurrentCUDAStream().stream();
   if (qtype == 0)
     om::dispatch<om::WQ_Q4>(bx, swap, tx, g, grid, st);
   else
     om::dispatch<om::WQ_I8>(bx, swap, tx, g, grid, st);
-  if (splits > 1 && !fused_reduce)
+  if (splits > 1)
     om::launch_splitk_reduce(ws, splits, M, N, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), rp,
                              qtype == 1 ? scales->data_ptr<float>() : nullptr, st, has_peer ? &po : nullptr);
 }

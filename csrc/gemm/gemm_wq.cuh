@@ -50,11 +50,12 @@
 // weight stream. SWAP = false (prefill):
 // A = activations (128 tokens), B = weight tile (N = 128 weight rows).
 //
-// Q4 element decode per pair: prmt the two source bytes into the two bf16
-// halves, mask a nibble and OR the exponent of 128.0 (exact 128 + q), subtract
-// 136 (exact), multiply by the block scale (one rounding).
-// I8 element decode: fp32 magic-number conversion (exact), then packed
-// conversion to bf16 (exact); the per-row scale is applied in the epilogue.
+// Q4 element decode per pair (q4_pair): mask two nibbles of one word and OR the
+// exponent of 128.0 (exact 128 + q), subtract 136 (exact), multiply by the block
+// scale (one rounding). I8 element decode (i8_pair): fp32 magic-number
+// conversion (exact), then packed conversion to bf16 (exact); the per-row scale
+// is applied in the epilogue. Decode with M <= 128 tokens uses the TMEM-operand
+// kernel of gemm_wq_dec.cuh; this kernel serves larger M and prefill.
 #pragma once
 #include <cuda.h>
 #include "gemm_common.cuh"
@@ -84,11 +85,7 @@ struct WqCfg {
   static constexpr int XS = XSLOT <= 16384 ? 3 : 2;
   static constexpr int RAW_AVAIL = 208 * 1024 - WD * W_BYTES - XS * XSLOT;
   static constexpr int RD_ = RAW_AVAIL / RAW_BYTES > 24 ? 24 : RAW_AVAIL / RAW_BYTES;
-#ifdef OM_WQ_RD_CAP
-  static constexpr int RD = (RD_ < OM_WQ_RD_CAP ? RD_ : OM_WQ_RD_CAP) - (RD_ < OM_WQ_RD_CAP ? RD_ : OM_WQ_RD_CAP) % 4;
-#else
   static constexpr int RD = RD_ - RD_ % 4;        // multiple of NG and of every chunk size
-#endif
   static_assert(RD >= 8, "raw ring too shallow");
   static_assert(WD % NG == 0 && RPW % 16 == 0 && RD % CHMAX == 0, "ring / group shape");
   static constexpr int X_OFF = WD * W_BYTES;
@@ -97,35 +94,42 @@ struct WqCfg {
   static constexpr int SMEM_BYTES = BAR_OFF + (2 * WD + 2 * XS + 2 * RD + 4) * 8 + 16 + 1024;
 };
 
-__device__ __forceinline__ uint32_t q4_pair(uint32_t t, int shift, uint32_t s2) {
-  uint32_t v = ((t >> shift) & 0x000F000Fu) | 0x43004300u;
+// One pair of 4-bit values (bits 0-3 and 16-19 of t) -> bf16x2 (q - 8) * s:
+// (t & 0x000F000F) | bf16x2(128, 128) is exactly 128 + q per half, minus 136 is
+// exact, and the scale multiply rounds once.
+__device__ __forceinline__ uint32_t q4_pair(uint32_t t, uint32_t s2) {
+  uint32_t v;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(t));  // (t & m) | c
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   const uint32_t off = 0x43084308u;  // bf16x2(136, 136)
   b = __hsub2(b, *reinterpret_cast<const __nv_bfloat162*>(&off));
   b = __hmul2(b, *reinterpret_cast<const __nv_bfloat162*>(&s2));
   return *reinterpret_cast<uint32_t*>(&b);
 }
-
-// 8 packed bytes (lo nibbles or hi nibbles) -> one 16-byte chunk of 8 bf16
-__device__ __forceinline__ uint4 q4_chunk(uint32_t w0, uint32_t w1, int shift, uint32_t s2) {
+// One Q4 word of the device format (k = 8w .. 8w+7: k = 8w+2i in bits [4i, 4i+4),
+// k = 8w+2i+1 in bits [16+4i, 16+4i+4)) -> 8 consecutive bf16.
+__device__ __forceinline__ uint4 q4_word(uint32_t w, uint32_t s2) {
   uint4 o;
-  o.x = q4_pair(__byte_perm(w0, 0, 0x4140), shift, s2);
-  o.y = q4_pair(__byte_perm(w0, 0, 0x4342), shift, s2);
-  o.z = q4_pair(__byte_perm(w1, 0, 0x4140), shift, s2);
-  o.w = q4_pair(__byte_perm(w1, 0, 0x4342), shift, s2);
+  o.x = q4_pair(w, s2);
+  o.y = q4_pair(w >> 4, s2);
+  o.z = q4_pair(w >> 8, s2);
+  o.w = q4_pair(w >> 12, s2);
   return o;
 }
-
-__device__ __forceinline__ float i8_at(uint32_t w, int byte) {
-  const uint32_t u = ((w >> (8 * byte)) ^ 0x80u) & 0xFFu;
-  return __uint_as_float(0x4B000000u | u) - 8388736.f;
+// Two offset-binary INT8 bytes (q + 128; bytes b0 and b0 + 1 of w) -> bf16x2 of q:
+// the byte goes into the mantissa of 2^23 (exact), minus 2^23 + 128 (exact), then a
+// packed conversion (exact for |q| <= 128).
+__device__ __forceinline__ uint32_t i8_pair(uint32_t w, int b0) {
+  const float lo = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 + b0)) - 8388736.f;
+  const float hi = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7651 + b0)) - 8388736.f;
+  return pack_bf16x2(lo, hi);
 }
 __device__ __forceinline__ uint4 i8_chunk(uint32_t w0, uint32_t w1) {
   uint4 o;
-  o.x = pack_bf16x2(i8_at(w0, 0), i8_at(w0, 1));
-  o.y = pack_bf16x2(i8_at(w0, 2), i8_at(w0, 3));
-  o.z = pack_bf16x2(i8_at(w1, 0), i8_at(w1, 1));
-  o.w = pack_bf16x2(i8_at(w1, 2), i8_at(w1, 3));
+  o.x = i8_pair(w0, 0);
+  o.y = i8_pair(w0, 2);
+  o.z = i8_pair(w1, 0);
+  o.w = i8_pair(w1, 2);
   return o;
 }
 
@@ -160,8 +164,6 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* tfull = raw_empty + RD;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  __shared__ int s_last;            // split-K finisher flag of the current unit (epilogue warps)
-  __shared__ uint64_t fin_bar[2];   // epilogue-warp rendezvous of the finisher (bounded waits)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -184,7 +186,6 @@ __global__ void __launch_bounds__(512, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
-      mbar_init(&fin_bar[a], 128);
     }
     fence_barrier_init();
   }
@@ -247,7 +248,6 @@ __global__ void __launch_bounds__(512, 1)
         for (int kb = kb0; kb < kb1; kb += CH, ++ix) {
           const int s = ix % XS;
           if (!mbar_wait(&x_empty[s], ((ix / XS) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
-          if (g.dbg & 32) { mbar_arrive(&x_full[s]); continue; }
           mbar_arrive_expect_tx(&x_full[s], CH * C::X_BYTES);
           // 3-D box {64 k, BX rows, CH k-blocks}: CH swizzled [BX][64] tiles back to back
           tma_load_3d(xbuf + s * C::XSLOT, &tmX, &x_full[s], 0, xt * BX, kb);
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(512, 1)
             const uint32_t d_tmem = tmem_base + (acc * RMAX + j) * BN_MMA;
             for (int kk = 0; kk < CH; ++kk, ++it) {
               const int ws = it % WD;
-              if (!(g.dbg & 8) && !mbar_wait(&w_ready[ws], (it / WD) & 1, g.status, OM_ERR_WAIT_FULL)) {
+              if (!mbar_wait(&w_ready[ws], (it / WD) & 1, g.status, OM_ERR_WAIT_FULL)) {
                 ok = false;
                 break;
               }
@@ -291,16 +291,14 @@ __global__ void __launch_bounds__(512, 1)
               const uint32_t b_addr = SWAP ? x_addr : w_addr;
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                if (g.dbg & 1) break;
                 tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32, 1024), smem_desc_sw128(b_addr + k * 32, 1024),
                            IDESC, (kb > kb0 || kk > 0 || k > 0) ? 1u : 0u);
               }
-              if (!(g.dbg & 8)) tc_commit(&w_empty[ws]);
+              tc_commit(&w_empty[ws]);
             }
           }
           if (ok) {
-            if (g.dbg & 32) mbar_arrive(&x_empty[xs]);
-            else tc_commit(&x_empty[xs]);
+            tc_commit(&x_empty[xs]);
           }
         }
         if (ok) tc_commit(&tfull[acc]);
@@ -326,14 +324,12 @@ __global__ void __launch_bounds__(512, 1)
       for (int t = 0; t < nT; ++t, ++it) {
         if (it % NG != grp) continue;
         const int r = it % RD, s = it % WD;
-        if (!((g.dbg & 4) ? mbar_wait_sleep(&raw_full[r / CH], (it / RD) & 1, 200, g.status, OM_ERR_WAIT_FULL)
-                          : mbar_wait(&raw_full[r / CH], (it / RD) & 1, g.status, OM_ERR_WAIT_FULL))) { ok = false; break; }
+        if (!mbar_wait(&raw_full[r / CH], (it / RD) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
         const uint32_t raw = raw_s + r * C::RAW_BYTES;
         uint4 p0[NP] = {}, p1[NP] = {};
         uint32_t s2[NP] = {};
 #pragma unroll
         for (int j = 0; j < NP; ++j) {
-          if (g.dbg & 16) break;
           const int row = wi * RPW + j * 16 + (lane >> 1);
           if (QT == WQ_Q4) {
             // block `half` of the row: 16 bytes of nibbles (32 values) and its scale
@@ -344,20 +340,18 @@ __global__ void __launch_bounds__(512, 1)
             p1[j] = lds128(raw + row * 64 + half * 32 + 16);
           }
         }
-        if (!(g.dbg & 8) && !((g.dbg & 4) ? mbar_wait_sleep(&w_empty[s], ((it / WD) & 1) ^ 1, 200, g.status, OM_ERR_WAIT_EMPTY)
-                          : mbar_wait(&w_empty[s], ((it / WD) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY))) { ok = false; break; }
+        if (!mbar_wait(&w_empty[s], ((it / WD) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
 #pragma unroll
         for (int j = 0; j < NP; ++j) {
-          if (g.dbg & 2) break;
           const int row = wi * RPW + j * 16 + (lane >> 1);
           const uint32_t sw = row & 7;
           const uint32_t wrow = w_s + s * C::W_BYTES + row * 128;
           const uint32_t c0 = 4 * half;
           if (QT == WQ_Q4) {
-            sts128(wrow + (((c0 + 0) ^ sw) << 4), q4_chunk(p0[j].x, p0[j].y, 0, s2[j]));
-            sts128(wrow + (((c0 + 1) ^ sw) << 4), q4_chunk(p0[j].z, p0[j].w, 0, s2[j]));
-            sts128(wrow + (((c0 + 2) ^ sw) << 4), q4_chunk(p0[j].x, p0[j].y, 4, s2[j]));
-            sts128(wrow + (((c0 + 3) ^ sw) << 4), q4_chunk(p0[j].z, p0[j].w, 4, s2[j]));
+            sts128(wrow + (((c0 + 0) ^ sw) << 4), q4_word(p0[j].x, s2[j]));
+            sts128(wrow + (((c0 + 1) ^ sw) << 4), q4_word(p0[j].y, s2[j]));
+            sts128(wrow + (((c0 + 2) ^ sw) << 4), q4_word(p0[j].z, s2[j]));
+            sts128(wrow + (((c0 + 3) ^ sw) << 4), q4_word(p0[j].w, s2[j]));
           } else {
             sts128(wrow + (((c0 + 0) ^ sw) << 4), i8_chunk(p0[j].x, p0[j].y));
             sts128(wrow + (((c0 + 1) ^ sw) << 4), i8_chunk(p0[j].z, p0[j].w));
@@ -365,11 +359,11 @@ __global__ void __launch_bounds__(512, 1)
             sts128(wrow + (((c0 + 3) ^ sw) << 4), i8_chunk(p1[j].z, p1[j].w));
           }
         }
-        if (!(g.dbg & 128)) fence_proxy_async_smem();
+        fence_proxy_async_smem();
         __syncwarp();
         // the raw slot is released only after every lane has read its part
         if (lane == 0) {
-          if (!(g.dbg & 8)) mbar_arrive(&w_ready[s]);
+          mbar_arrive(&w_ready[s]);
           mbar_arrive(&raw_empty[r]);
         }
       }
@@ -377,16 +371,15 @@ __global__ void __launch_bounds__(512, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    int local = 0, nfin = 0;
+    int local = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
       int tr, tc, sp;
       unit_coords(g, u, tr, tc, sp);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!((g.dbg & 4) ? mbar_wait_sleep(&tfull[acc], aph, 2000, g.status, OM_ERR_WAIT_ACCUM)
-                        : mbar_wait(&tfull[acc], aph, g.status, OM_ERR_WAIT_ACCUM))) break;
+      if (!mbar_wait(&tfull[acc], aph, g.status, OM_ERR_WAIT_ACCUM)) break;
       tc_fence_after();
-      const int nR = (g.dbg & 64) ? 0 : unit_rows(g, tr);
+      const int nR = unit_rows(g, tr);
       for (int j = 0; j < nR; ++j) {
         const int wt = SWAP ? tr * g.rgroup + j : tr;
         const int r = wt * 128 + q * 32 + lane;
@@ -401,31 +394,6 @@ __global__ void __launch_bounds__(512, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
-      if (g.sem != nullptr && g.splits > 1) {
-        // in-kernel split-K reduction: the CTA that completes a tile's last split finishes it
-        __threadfence();  // this thread's partial stores, visible device-wide
-        mbar_arrive(&fin_bar[0]);
-        if (!mbar_wait(&fin_bar[0], nfin & 1, g.status, OM_ERR_WAIT_ACCUM)) break;
-        if (q == 0 && lane == 0) {
-          const int tile = tr * g.tiles_c + tc;
-          const int prev = atomicAdd(&g.sem[tile], 1);
-          s_last = prev == g.splits - 1;
-          if (s_last) g.sem[tile] = 0;  // ready for the next launch
-        }
-        mbar_arrive(&fin_bar[1]);
-        if (!mbar_wait(&fin_bar[1], nfin & 1, g.status, OM_ERR_WAIT_ACCUM)) break;
-        ++nfin;
-        if (s_last) {
-          __threadfence();
-          const int nRf = unit_rows(g, tr);
-          for (int j = 0; j < nRf; ++j) {
-            const int wt = SWAP ? tr * g.rgroup + j : tr;
-            const int r = wt * 128 + q * 32 + lane;
-#pragma unroll 1
-            for (int cc = 0; cc < BN_MMA / 32; ++cc) splitk_finish_chunk(g, r, tc * BN_MMA + cc * 32);
-          }
-        }
-      }
     }
   }
 

@@ -128,6 +128,49 @@ OPENMINI_API openmini_error_t openmini_get_stats(const openmini_context_t* ctx, 
 OPENMINI_API void openmini_reset_stats(openmini_context_t* ctx);
 OPENMINI_API openmini_error_t openmini_set_log_callback(openmini_log_callback_t callback, void* user_data);
 
+/* ---------------------------------------------------------------------------
+ * Allocation-free paged attention (exported by the CUDA kernel library
+ * openmini_v1_b200/_C*.so, not by the runtime library above). It has no
+ * counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: code running inside a
+ * custom allocator or memory-pool hook, plugins hosted by a runtime that owns
+ * all device memory, and real-time paths where a cudaMalloc could block. The
+ * caller passes only inputs and outputs; the split-KV partials live in one
+ * fixed device array of OM_NOALLOC_SCRATCH_FLOATS fp32 values (16 MiB) that
+ * every GPU loading the library holds until the process exits.
+ *
+ *   q            bf16 [rows, Hq, head_dim], row stride q_ld elements
+ *   k/v_cache    bf16 [num_blocks, Hkv, 16, head_dim] (16-token pages)
+ *   block_tables int32 [num_seqs, max_blocks]
+ *   row_seq      int32 [rows] sequence of each query row
+ *   row_ctx      int32 [rows] visible keys of each row (<= max_ctx)
+ *   out          bf16 [rows, Hq, head_dim], row stride out_ld elements
+ *   status       optional device int32; a bad block id, sequence index or a
+ *                context past max_ctx / the block table sets it to 5
+ *                (the access is skipped or clamped)
+ * head_dim is 64 or 128; Hq / Hkv is 1, 2, 4, 5, 8 or 16.
+ * A call needs rows * Hq * ceil(max_ctx / 512) * (head_dim + 2) floats of the
+ * array; larger requests return OM_NOALLOC_TOO_LARGE. The first call on a
+ * device looks up the array's address with that device current; make it
+ * before any stream capture. Every call shares the array, so calls that
+ * overlap on the GPU (other streams, other host threads) race: serialise them.
+ * No cudaMalloc, cudaFree or allocating library routine is called.
+ * ------------------------------------------------------------------------- */
+#define OM_NOALLOC_SCRATCH_FLOATS (4u << 20)
+enum {
+  OM_NOALLOC_OK = 0,
+  OM_NOALLOC_TOO_LARGE = 1,   /* request exceeds the fixed scratch array */
+  OM_NOALLOC_BAD_ARGS = 2,    /* unsupported head_dim / GQA group / null pointer / bad size */
+  OM_NOALLOC_CUDA_ERROR = 3,  /* symbol lookup or kernel launch failed */
+};
+struct CUstream_st;
+OPENMINI_API int om_paged_attention_noalloc(const void* q, int q_ld, const void* k_cache, const void* v_cache,
+                                            int num_blocks, int Hkv, int head_dim, const int* block_tables,
+                                            int num_seqs, int max_blocks, const int* row_seq, const int* row_ctx,
+                                            int rows, void* out, int out_ld, int Hq, int max_ctx, float scale,
+                                            int* status, struct CUstream_st* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,8 +61,7 @@ class DecodeGraphs:
     def _body(self, B):
         m = self.eng.model
         x = m(self._fb(B), self.eng.kv)
-        lg = m.logits(x)
-        return ops.sample(lg, self.temp[:B], self.top_p[:B], self.top_k[:B], self.rng[:B], False)[:2]
+        return m.sample(x, self.temp[:B], self.top_p[:B], self.top_k[:B], self.rng[:B], False)[:2]
 
     def capture(self, B: int):
         eng = self.eng

@@ -208,7 +208,9 @@ class LLMEngine:
     def _sync_bm_tokens(self, r: Request):
         n = self.bm.seq_len(r.seq_id)
         if n < r.num_tokens:
-            self._apply_cow(self.bm.append(r.seq_id, r.all_token_ids[n:]))
+            cow = self.bm.append(r.seq_id, r.token_slice(n, r.num_tokens))
+            if cow:
+                self._apply_cow(cow)
 
     # ---------------------------------------------------------------- multi-step decode
     def begin_multi_decode(self, n: int):
@@ -311,8 +313,7 @@ class LLMEngine:
         for si, c in enumerate(chunks):
             r = c.req
             n = c.end - c.start
-            toks = r.all_token_ids
-            ids[o:o + n] = toks[c.start:c.end]
+            ids[o:o + n] = r.token_slice(c.start, c.end)
             pos[o:o + n] = np.arange(c.start, c.end, dtype=np.int32)
             slots[o:o + n] = self.bm.slots(r.seq_id, c.start, c.end)
             rseq[o:o + n] = si
@@ -353,6 +354,9 @@ class LLMEngine:
 
     def _forward_sample(self, fb, samp, rows_req):
         x = self.model(fb, self.kv)
+        want_mask = any(r.params.return_sampling_mask for r in rows_req)
+        if all(r.params.repetition_penalty == 1.0 for r in rows_req):
+            return self.model.sample(x, samp["temperature"], samp["top_p"], samp["top_k"], samp["rng"], want_mask)
         logits = self.model.logits(x)
         if any(r.params.repetition_penalty != 1.0 for r in rows_req):
             L = max(1, max(len(r.all_token_ids) for r in rows_req))
@@ -363,7 +367,6 @@ class LLMEngine:
             pen = torch.tensor([r.params.repetition_penalty for r in rows_req], dtype=torch.float32)
             logits = logits.float()
             ops.repetition_penalty(logits, prev.to(self.device), pen.to(self.device))
-        want_mask = any(r.params.return_sampling_mask for r in rows_req)
         return ops.sample(logits, samp["temperature"], samp["top_p"], samp["top_k"], samp["rng"], want_mask)
 
     def _commit(self, so, rows_req, tok, lp, mask):

@@ -52,7 +52,7 @@ class RequestStatus(enum.Enum):
 _ids = itertools.count()
 
 
-@dataclass
+@dataclass(eq=False)  # identity semantics: requests are compared and hashed by object
 class Request:
     request_id: str
     prompt_token_ids: list
@@ -75,6 +75,15 @@ class Request:
     @property
     def all_token_ids(self):
         return self.prompt_token_ids + self.output_token_ids
+
+    def token_slice(self, start: int, end: int) -> list:
+        """all_token_ids[start:end] without concatenating the whole prompt."""
+        P = len(self.prompt_token_ids)
+        if start >= P:
+            return self.output_token_ids[start - P:end - P]
+        if end <= P:
+            return self.prompt_token_ids[start:end]
+        return self.prompt_token_ids[start:] + self.output_token_ids[:end - P]
 
     @property
     def num_tokens(self):

@@ -138,19 +138,21 @@ class Scheduler:
             return out
         # 3) decode every running request (one token each)
         decode = [r for r in self.running if not r.in_prefill]
-        for r in list(decode):
-            if r not in self.running:
+        gone = set()  # preempted this step (requests hash by identity)
+        for r in decode:
+            if r in gone:
                 continue
             while not self.bm.can_append(r.seq_id, 1):
                 v = self._victim(r)
                 if v is None:
                     break
                 self._preempt(v, out)
-                if v in decode:
-                    decode.remove(v)
+                gone.add(v)
             if not self.bm.can_append(r.seq_id, 1):
                 self._preempt(r, out)
-                decode.remove(r)
+                gone.add(r)
+        if gone:
+            decode = [r for r in decode if r not in gone]
         for r in decode:
             pos = r.num_tokens - 1
             out.chunks.append(ScheduledChunk(r, pos, pos + 1, True))

@@ -290,6 +290,36 @@ class DecoderLM(nn.Module):
             return h, None
         return h, self._tp_sum(ops.linear(act, L["down"]))
 
+    def sample(self, x: torch.Tensor, temperature, top_p, top_k, rng, want_mask: bool = False):
+        """LM head + sampler -> (tokens int32 [B], logprob fp32 [B], packed keep mask or None).
+
+        Under tensor parallelism with a vocabulary-sharded LM head the rows are sampled
+        row-parallel instead of gathering every rank's logits everywhere: one all-to-all
+        gives rank r the full-vocabulary logits of rows [r B'/W, (r+1) B'/W) (B' = B
+        padded to a multiple of W), each rank samples only those rows (global row index
+        in the random counter, so draws match an unsplit run), and one all-gather of
+        (token, logprob) pairs returns the result to every rank. Per rank this moves
+        1/W of the logits and does 1/W of the sampling work."""
+        W = self.par.tp
+        if W == 1 or self.vocab_local == self.cfg.vocab_size or want_mask:
+            return ops.sample(self.logits(x), temperature, top_p, top_k, rng, want_mask)
+        B = x.shape[0]
+        Bp = (B + W - 1) // W * W
+        per = Bp // W
+        lg = ops.linear(x, self.lm_head)  # [B, V / W]
+        knobs = [temperature, top_p, top_k, rng]
+        if Bp > B:
+            lg = torch.cat([lg, lg.new_zeros(Bp - B, lg.shape[1])])
+            knobs = [torch.cat([k, k[:1].expand(Bp - B, *k.shape[1:])]) for k in knobs]
+        recv = self._comm.all_to_all(lg.view(W, per, -1))  # [src rank, my rows, src vocab shard]
+        full = recv.permute(1, 0, 2).reshape(per, -1)
+        r = self.par.tp_rank
+        rows = slice(r * per, (r + 1) * per)
+        tok, lp, _ = ops.sample(full, *(k[rows] for k in knobs), want_mask=False, row0=r * per)
+        pair = torch.stack([tok, lp.view(torch.int32)], dim=1)  # [per, 2] int32
+        allp = self._comm.all_gather(pair, dim=0)  # [Bp, 2]
+        return allp[:B, 0].contiguous(), allp[:B, 1].contiguous().view(torch.float32), None
+
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         lg = ops.linear(x, self.lm_head)
         if self.par.tp > 1 and self.vocab_local != self.cfg.vocab_size:

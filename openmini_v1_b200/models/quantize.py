@@ -15,8 +15,6 @@ on the CPU. Reference formats: openmini-server/src/model/inference/quant.rs:56-4
 """
 from __future__ import annotations
 
-import os
-
 import torch
 
 from .. import _native, ops
@@ -31,37 +29,67 @@ def _pad_rows(t: torch.Tensor, mult: int = 128) -> torch.Tensor:
     return torch.cat([t, torch.zeros(pad, *t.shape[1:], dtype=t.dtype, device=t.device)])
 
 
-def tile_q4(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
-    """Row-major nibbles [N, K/2] + bf16 scales [N, K/32] -> tiles uint8 [ceil(N/128), K/64, 4608].
+def _ggml_to_tile_order(q: torch.Tensor) -> torch.Tensor:
+    """Nibbles in ggml Q4_0 order ([rows, K/2]: byte j of a 32-block = element j low,
+    element j + 16 high) -> the device order: per 8 consecutive elements one 32-bit
+    word with element 2i in bits [4i, 4i+4) and element 2i+1 in bits [16+4i, 16+4i+4),
+    so one mask of the word yields a bf16x2 pair of neighbouring elements."""
+    rows, k2 = q.shape
+    blk = q.view(rows, k2 // 16, 16)
+    e = torch.cat([blk & 15, blk >> 4], dim=2).view(rows, k2 // 4, 8)  # [rows, K/8, 8] elements
+    b0 = e[..., 0] | (e[..., 2] << 4)
+    b1 = e[..., 4] | (e[..., 6] << 4)
+    b2 = e[..., 1] | (e[..., 3] << 4)
+    b3 = e[..., 5] | (e[..., 7] << 4)
+    return torch.stack([b0, b1, b2, b3], dim=2).view(rows, k2)
 
-    Tile (rt, kb) = 128 rows x 32 bytes of nibbles (K block kb) followed by the
-    2 x 128 bf16 scales of its two 32-blocks, scale index = block * 128 + row."""
+
+def _tile_to_ggml_order(t: torch.Tensor) -> torch.Tensor:
+    """Inverse of :func:`_ggml_to_tile_order`."""
+    rows, k2 = t.shape
+    w = t.view(rows, k2 // 4, 4)
+    e = torch.stack([w[..., 0] & 15, w[..., 2] & 15, w[..., 0] >> 4, w[..., 2] >> 4,
+                     w[..., 1] & 15, w[..., 3] & 15, w[..., 1] >> 4, w[..., 3] >> 4], dim=2)
+    e = e.reshape(rows, k2 // 16, 32)
+    return (e[..., :16] | (e[..., 16:] << 4)).reshape(rows, k2)
+
+
+def tile_q4(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """ggml-order nibbles [N, K/2] + bf16 scales [N, K/32] -> tiles uint8 [ceil(N/128), K/64, 4608].
+
+    Tile (rt, kb) = 128 rows x 32 bytes of nibbles (K block kb, device nibble order,
+    see :func:`_ggml_to_tile_order`) followed by the 2 x 128 bf16 scales of its two
+    32-blocks, scale index = block * 128 + row."""
     N, K2 = q.shape
     KB = K2 // 32
-    qp = _pad_rows(q).view(-1, 128, KB, 32).permute(0, 2, 1, 3).contiguous().view(-1, KB, 4096)
+    qd = _ggml_to_tile_order(q.contiguous())
+    qp = _pad_rows(qd).view(-1, 128, KB, 32).permute(0, 2, 1, 3).contiguous().view(-1, KB, 4096)
     sp = _pad_rows(scales.view(torch.int16)).view(-1, 128, KB, 2).permute(0, 2, 3, 1).contiguous()
     sp = sp.view(torch.uint8).view(-1, KB, 512)
     return torch.cat([qp, sp], dim=2).contiguous()
 
 
 def untile_q4(tiles: torch.Tensor, N: int):
-    """Inverse of :func:`tile_q4`: (nibbles uint8 [N, K/2], bf16 scales [N, K/32])."""
+    """Inverse of :func:`tile_q4`: (ggml-order nibbles uint8 [N, K/2], bf16 scales [N, K/32])."""
     NT, KB, _ = tiles.shape
     q = tiles[:, :, :4096].reshape(NT, KB, 128, 32).permute(0, 2, 1, 3).reshape(NT * 128, KB * 32)[:N]
     s = tiles[:, :, 4096:].contiguous().view(torch.int16).view(NT, KB, 2, 128).permute(0, 3, 1, 2)
     s = s.reshape(NT * 128, KB * 2)[:N].contiguous().view(torch.bfloat16)
-    return q.contiguous(), s
+    return _tile_to_ggml_order(q.contiguous()), s
 
 
 def tile_i8(q: torch.Tensor) -> torch.Tensor:
+    """int8 [N, K] -> tiles uint8 [ceil(N/128), K/64, 8192] of offset-binary bytes (q + 128)."""
     N, K = q.shape
     KB = K // 64
-    return _pad_rows(q.view(torch.uint8)).view(-1, 128, KB, 64).permute(0, 2, 1, 3).contiguous().view(-1, KB, 8192)
+    ob = q.view(torch.uint8) ^ 0x80
+    return _pad_rows(ob).view(-1, 128, KB, 64).permute(0, 2, 1, 3).contiguous().view(-1, KB, 8192)
 
 
 def untile_i8(tiles: torch.Tensor, N: int) -> torch.Tensor:
     NT, KB, _ = tiles.shape
-    return tiles.view(NT, KB, 128, 64).permute(0, 2, 1, 3).reshape(NT * 128, KB * 64)[:N].contiguous().view(torch.int8)
+    ob = tiles.view(NT, KB, 128, 64).permute(0, 2, 1, 3).reshape(NT * 128, KB * 64)[:N]
+    return (ob ^ 0x80).contiguous().view(torch.int8)
 
 
 class Q4Weight:
@@ -174,9 +202,6 @@ class Int8Weight:
         return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid, peer)
 
 
-_FUSED_SPLITK = os.environ.get("OM_WQ_FUSED_SPLITK", "0") == "1"
-
-
 def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
@@ -186,9 +211,8 @@ def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     c = ops.ctx(x.device)
     ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    # The in-kernel split-K finisher (``sem``) is correct but measured ~3.7x slower on the
-    # decode GEMMs, so the separate reduction kernel stays unless OM_WQ_FUSED_SPLITK=1.
-    kw = {"sem": c.semaphores()} if _FUSED_SPLITK else {}
+    # decode (M <= 128) runs the stream-K kernel: its per-group counters are ``sem``
+    kw = {"sem": c.semaphores()}
     if peer is not None:
         kw["peer"] = peer
     _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status, **kw)

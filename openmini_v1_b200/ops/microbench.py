@@ -160,6 +160,11 @@ SUITE = {
     "gemm_q4_decode_gateup": (case_gemm, dict(m=32, n=57344, k=8192, kind="q4")),
     "gemm_q4_decode_down": (case_gemm, dict(m=32, n=8192, k=28672, kind="q4")),
     "gemm_i8_decode_qkv": (case_gemm, dict(m=32, n=10240, k=8192, kind="int8")),
+    "gemm_i8_decode_gateup": (case_gemm, dict(m=32, n=57344, k=8192, kind="int8")),
+    # per-GPU gate/up shapes under TP 2 / 4 / 8 with 32 requests per GPU (weak scaling)
+    "gemm_q4_decode_gateup_tp2": (case_gemm, dict(m=64, n=28672, k=8192, kind="q4")),
+    "gemm_q4_decode_gateup_tp4": (case_gemm, dict(m=128, n=14336, k=8192, kind="q4")),
+    "gemm_q4_decode_gateup_tp8": (case_gemm, dict(m=256, n=7168, k=8192, kind="q4")),
     "gemm_bf16_prefill": (case_gemm, dict(m=4096, n=8192, k=8192, kind="bf16")),
     "gemm_q4_prefill": (case_gemm, dict(m=4096, n=8192, k=8192, kind="q4")),
     "attn_decode_tc": (case_decode_attn, dict(batch=32, ctx=4096, hq=64, hkv=8)),

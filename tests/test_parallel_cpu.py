@@ -111,3 +111,62 @@ def test_expert_parallel_matches_single_rank():
     for rank, err, same in _run(_ep_worker):
         assert same
         assert err < 1e-4, (rank, err)
+
+
+def _tp_sample_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from openmini_v1_b200 import ops
+        from openmini_v1_b200.models.config import tiny
+        from openmini_v1_b200.models.llama import DecoderLM
+        from openmini_v1_b200.parallel.comm import CollectiveOps
+        from openmini_v1_b200.parallel.state import ParallelState
+        cfg = tiny()
+        par = ParallelState.build(tp=world)
+        m = DecoderLM(cfg, par=par, device="cpu", seed=3)
+        m.set_comm(CollectiveOps(par.tp_group))
+        assert m.vocab_local * world == cfg.vocab_size  # the vocabulary-sharded head
+        res = []
+        for B in (5, 8):  # 5: padded to a multiple of the TP size
+            g = torch.Generator().manual_seed(B)
+            x = torch.randn(B, cfg.hidden_size, generator=g)
+            temp = torch.rand(B, generator=g) + 0.3
+            temp[0] = 0.0  # one greedy row
+            top_p = torch.rand(B, generator=g) * 0.5 + 0.5
+            top_k = torch.tensor([0, 5] * B, dtype=torch.int32)[:B]
+            rng = torch.randint(0, 1 << 30, (B, 2), generator=g)
+            want_t, want_lp, _ = ops.sample(m.logits(x), temp, top_p, top_k, rng)
+            got_t, got_lp, _ = m.sample(x, temp, top_p, top_k, rng)
+            res.append((got_t.tolist() == want_t.tolist(), float((got_lp - want_lp).abs().max())))
+        q.put((rank, res))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_row_parallel_sampling_matches_gathered_logits():
+    """Row-parallel sampling under TP (all-to-all of vocab shards, each rank samples its
+    rows, all-gather of tokens) draws exactly what sampling the gathered logits draws."""
+    world = 2
+    q = mp.get_context("spawn").Queue()
+    procs = [mp.get_context("spawn").Process(target=_tp_sample_worker, args=(r, world, _free_port_shared(), q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res in out:
+        for same, lp_err in res:
+            assert same and lp_err < 1e-5, (rank, res)
+
+
+_PORT = None
+
+
+def _free_port_shared():
+    global _PORT
+    if _PORT is None:
+        _PORT = _free_port()
+    return _PORT
