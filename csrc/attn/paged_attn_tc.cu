@@ -44,13 +44,22 @@ struct AttnTcArgs {
   int items;    // rows * Hkv * NP
 };
 
+// Items are numbered partition-major: all (row, KV head) pairs of partition 0, then of
+// partition 1, ... Partitions past a row's context are empty, and short rows only
+// fill the low partitions, so with the partition varying fastest the round-robin
+// deal gave some CTAs only empty items and others only full ones; partition-major
+// numbering gives every CTA the same mix.
 __device__ __forceinline__ void item_coords(const AttnTcArgs& t, int it, int& row, int& kvh, int& part) {
-  part = it % t.a.NP;
-  const int r = it / t.a.NP;
+  const int per_part = t.items / t.a.NP;  // rows * Hkv
+  part = it / per_part;
+  const int r = it - part * per_part;
   kvh = r % t.a.Hkv;
   row = r / t.a.Hkv;
 }
 
+// NH: query heads handled per KV head in the softmax (G rounded up to 8 or 16; the
+// MMA always computes 16 columns, the padded ones are never read).
+template <int NH>
 __global__ void __launch_bounds__(256, 1)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const __grid_constant__ CUtensorMap tmQ, const AttnTcArgs t) {
@@ -217,7 +226,7 @@ __global__ void __launch_bounds__(256, 1)
       const int end = min(ctx, start + ATT_PART);
       float m[16], l[16], acc[16];
 #pragma unroll
-      for (int h = 0; h < 16; ++h) {
+      for (int h = 0; h < NH; ++h) {
         m[h] = -INFINITY;
         l[h] = 0.f;
         acc[h] = 0.f;
@@ -234,10 +243,10 @@ __global__ void __launch_bounds__(256, 1)
         const bool valid = c0 + tid < end;
         float p[16], alpha[16];
 #pragma unroll
-        for (int h = 0; h < 16; ++h) p[h] = valid ? __uint_as_float(sr[h]) * a.scale_log2 : -INFINITY;
+        for (int h = 0; h < NH; ++h) p[h] = valid ? __uint_as_float(sr[h]) * a.scale_log2 : -INFINITY;
         // chunk max per head over the 128 keys
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
+        for (int h = 0; h < NH; ++h) {
           float v = p[h];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -245,7 +254,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         named_bar_sync(1, 128);
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
+        for (int h = 0; h < NH; ++h) {
           const float cm = fmaxf(fmaxf(red_max[h], red_max[16 + h]), fmaxf(red_max[32 + h], red_max[48 + h]));
           const float mn = fmaxf(m[h], cm);
           alpha[h] = exp2f(m[h] - mn);  // 0 when m was -inf
@@ -253,7 +262,7 @@ __global__ void __launch_bounds__(256, 1)
           p[h] = valid ? exp2f(p[h] - mn) : 0.f;
         }
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
+        for (int h = 0; h < NH; ++h) {
           float v = p[h];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(256, 1)
           uint8_t* ph = ps + (tid >> 6) * (P_BYTES / 2);
           const int kk = tid & 63;
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
+          for (int h = 0; h < NH; ++h) {
             const float v = h < t.G ? p[h] : 0.f;
             *reinterpret_cast<__nv_bfloat16*>(ph + h * 128 + ((((kk >> 3) ^ (h & 7))) << 4) + (kk & 7) * 2) =
                 __float2bfloat16_rn(v);
@@ -274,7 +283,7 @@ __global__ void __launch_bounds__(256, 1)
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
 #pragma unroll
-        for (int h = 0; h < 16; ++h)
+        for (int h = 0; h < NH; ++h)
           l[h] = l[h] * alpha[h] + (red_sum[h] + red_sum[16 + h] + red_sum[32 + h] + red_sum[48 + h]);
         mbar_arrive(p_full);
         // O chunk: thread = output dim
@@ -287,7 +296,7 @@ __global__ void __launch_bounds__(256, 1)
         mbar_arrive(o_empty);
         // the P ordering barrier above also keeps red_* stable until everyone read them
 #pragma unroll
-        for (int h = 0; h < 16; ++h) acc[h] = acc[h] * alpha[h] + __uint_as_float(orr[h]);
+        for (int h = 0; h < NH; ++h) acc[h] = acc[h] * alpha[h] + __uint_as_float(orr[h]);
       }
       if (!ok) break;
       const size_t pbase = ((size_t)row * a.Hq + (size_t)kvh * t.G) * a.NP + part;
@@ -295,7 +304,7 @@ __global__ void __launch_bounds__(256, 1)
       if (tid < t.G) {
         float mm = 0.f, ll = 0.f;
 #pragma unroll
-        for (int h = 0; h < 16; ++h)
+        for (int h = 0; h < NH; ++h)
           if (h == tid) { mm = m[h]; ll = l[h]; }
         a.part_ml[(pbase + (size_t)tid * a.NP) * 2 + 0] = mm;
         a.part_ml[(pbase + (size_t)tid * a.NP) * 2 + 1] = ll;
@@ -364,12 +373,17 @@ void om_paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
   int dev;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    OM_CUDA_CHECK(cudaFuncSetAttribute(om::paged_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    OM_CUDA_CHECK(cudaFuncSetAttribute(om::paged_attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    OM_CUDA_CHECK(cudaFuncSetAttribute(om::paged_attn_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES));
     attr_set[dev] = true;
   }
   const int grid = std::min(t.items, om::num_sms());
-  om::paged_attn_tc_kernel<<<grid, 256, SMEM_BYTES, st>>>(tk, tv, tq, t);
+  if (t.G <= 8)
+    om::paged_attn_tc_kernel<8><<<grid, 256, SMEM_BYTES, st>>>(tk, tv, tq, t);
+  else
+    om::paged_attn_tc_kernel<16><<<grid, 256, SMEM_BYTES, st>>>(tk, tv, tq, t);
   OM_LAUNCH_CHECK();
   om::attn_merge_kernel<128><<<dim3(rows, Hq), 128, 0, st>>>(a);
   OM_LAUNCH_CHECK();

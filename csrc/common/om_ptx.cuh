@@ -182,6 +182,12 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Untiled bulk prefetch global -> L2 (address and size 16-byte aligned): no shared
+// memory, no completion signal; a later copy of the same bytes then hits L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes)
+               : "memory");
+}
 // Shared-space loads / stores by 32-bit shared address (no generic-address
 // translation, short-scoreboard latency).
 __device__ __forceinline__ uint4 lds128(uint32_t a) {

@@ -77,6 +77,7 @@ struct GemmArgs {
   long long sk_total;
   int sk_nc;
   float* part;
+  int vec_out;       // output rows (and residual rows) 16-byte aligned: vector epilogue stores
 };
 
 // Row pointer of output row m (local Y, or the owner's slot in peer mode).

@@ -120,7 +120,7 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
 
   // ---------------------------------------------------------------- stream-K decode kernel
   const int dec_ch = qtype == 0 ? 4 : 2;
-  const int dec_r = bx == 32 ? 2 : 1;
+  const int dec_r = bx == 32 ? 2 : 1;  // = WqDecCfg<bx, *>::R
   if (swap && bx <= 128 && force_splits <= 0 && sem.has_value() && ws && g.num_kb % dec_ch == 0) {
     const int groups = (wt_tiles + dec_r - 1) / dec_r;
     const int nc = g.num_kb / dec_ch;
@@ -139,6 +139,15 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     g.out = out.data_ptr();
     g.resid = rp;
     if (has_peer) g.po = po;
+    {
+      bool v = (g.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0;
+      if (rp) v = v && (reinterpret_cast<uintptr_t>(rp) & 15) == 0;
+      if (has_peer) {
+        v = v && (po.peer_off & 15) == 0;
+        for (int i = 0; i < po.pworld; ++i) v = v && (reinterpret_cast<uintptr_t>(po.peer[i]) & 15) == 0;
+      }
+      g.vec_out = v ? 1 : 0;
+    }
     // activations as [K/64][M][64]: a box {64, bx, ch} is `ch` swizzled [bx][64] tiles
     CUtensorMap tx = om::make_tmap_3d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, K / 64, x.stride(0),
                                       64, 64, bx, dec_ch, CU_TENSOR_MAP_SWIZZLE_128B);

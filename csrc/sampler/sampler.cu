@@ -4,11 +4,10 @@
 // openmini-server/src/model/inference/model.rs:3970) sorts the vocabulary. Here
 // each row is handled by one thread-block cluster of SCL CTAs: every CTA keeps
 // its slice of the row in registers, and the top-k / top-p cut-offs are found
-// without sorting by a radix search over order-preserving keys of the logits
-// (16-bit keys for bf16 logits, 32-bit for fp32), 2 bits per pass: each pass
-// evaluates the 3 candidates of the next digit at once as count (top-k) or
-// probability-mass (top-p) sums over precomputed probabilities, combined across
-// the cluster through distributed shared memory in one exchange. Top-p keeps the smallest
+// without sorting by a bitwise binary search over order-preserving keys of the
+// logits (16-bit keys for bf16 logits, 32-bit for fp32): each probe is a plain
+// count (top-k) or probability-mass (top-p) reduction, combined across the
+// cluster through distributed shared memory. Top-p keeps the smallest
 // descending prefix whose mass reaches p (ties at the cut-off are kept), over
 // the top-k-restricted distribution. The draw is a Gumbel-max race among the
 // kept tokens with Philox-4x32-10 counter-based uniforms (Salmon et al.,
@@ -91,8 +90,6 @@ __device__ __forceinline__ unsigned long long ld_dsmem_u64(uint32_t addr) {
 }
 
 struct SampleSmem {
-  float vec_part[SNT / 32][16];  // cluster_reduce_vec: per-warp partials
-  float vec_slot[2][16];         // this CTA's partials, double-buffered by pass parity
   float warp_part[SNT / 32];
   float slot[2];                 // this CTA's partial, double-buffered by pass parity
   unsigned long long best_warp[SNT / 32];
@@ -131,74 +128,6 @@ __device__ __forceinline__ float cluster_reduce(float v, int op, SampleSmem& sm,
   return r;
 }
 
-// Sums of NV values over the cluster (every thread passes its NV partials and gets
-// the NV totals): one CTA-wide and one cluster-wide exchange for all NV values.
-template <int NV>
-__device__ __forceinline__ void cluster_reduce_vec(float (&v)[NV], float (*warp_part)[16], float (*slot)[16],
-                                                   int& pass) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
-  if (lane == 0)
-#pragma unroll
-    for (int i = 0; i < NV; ++i) warp_part[warp][i] = v[i];
-  __syncthreads();
-  const int buf = pass & 1;
-  if (threadIdx.x < NV) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < SNT / 32; ++w) t += warp_part[w][threadIdx.x];
-    slot[buf][threadIdx.x] = t;
-  }
-  cluster_sync();
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const uint32_t a = smem_u32(&slot[buf][i]);
-    float r = 0.f;
-#pragma unroll
-    for (int c = 0; c < SCL; ++c) r += ld_dsmem_f32(mapa(a, c));
-    v[i] = r;
-  }
-  ++pass;
-}
-
-// Largest key threshold t with S(t) >= target, where S(t) = sum of w over the
-// elements whose key >= t (monotone non-increasing in t), searched DB bits per
-// pass: each pass evaluates the 2^DB - 1 candidates of the next digit at once, so
-// a 16-bit search takes 16 / DB cluster reductions. `floor` is a lower bound
-// already known to satisfy the predicate.
-template <int EPT, int KEY_BITS, bool MASS, int DB>
-__device__ __forceinline__ uint32_t search_cut(const uint32_t (&key)[EPT], const float (&p)[EPT], float target,
-                                               uint32_t floor, float (*warp_part)[16], float (*slot)[16],
-                                               int& pass) {
-  constexpr int NC = (1 << DB) - 1;
-  uint32_t t = 0;
-  for (int sh = KEY_BITS - DB; sh >= 0; sh -= DB) {
-    float s[NC];
-#pragma unroll
-    for (int d = 0; d < NC; ++d) s[d] = 0.f;
-    const uint32_t hi = t >> sh;  // decided prefix (digit position zero)
-#pragma unroll
-    for (int e = 0; e < EPT; ++e) {
-      const uint32_t kh = key[e] >> sh;
-      // digit of the key relative to the prefix: below (none), inside, above (all)
-      const int dg = kh < hi ? -1 : (kh - hi > (uint32_t)NC ? NC : (int)(kh - hi));
-      const float w = MASS ? p[e] : 1.f;
-#pragma unroll
-      for (int d = 0; d < NC; ++d) s[d] += dg >= d + 1 ? w : 0.f;
-    }
-    cluster_reduce_vec<NC>(s, warp_part, slot, pass);
-    int best = 0;
-#pragma unroll
-    for (int d = 0; d < NC; ++d)
-      if (s[d] >= target || (t | ((uint32_t)(d + 1) << sh)) <= floor) best = d + 1;
-    t |= (uint32_t)best << sh;
-  }
-  return t;
-}
-
 template <typename T, int EPT>
 __global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel(const SampleArgs a) {
   __shared__ SampleSmem sm;
@@ -228,12 +157,8 @@ __global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel
   }
   const float mx = cluster_reduce(lmax, 1, sm, pass);
   float z = 0.f;
-  float p[EPT];  // unnormalised probabilities exp(x - mx)
 #pragma unroll
-  for (int e = 0; e < EPT; ++e) {
-    p[e] = __expf(x[e] - mx);
-    z += p[e];
-  }
+  for (int e = 0; e < EPT; ++e) z += __expf(x[e] - mx);
   z = cluster_reduce(z, 0, sm, pass);
 
   uint32_t cut = 1;  // keep key >= cut (real keys are >= 1)
@@ -250,19 +175,40 @@ __global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel
     }
   } else {
     const int k = a.top_k ? a.top_k[b] : 0;
-    if (k > 0 && k < V) cut = max(cut, search_cut<EPT, KEY_BITS, false, 2>(key, p, (float)k, 0u, sm.vec_part,
-                                                                         sm.vec_slot, pass));
-    const float tp = a.top_p ? a.top_p[b] : 1.f;
-    if (tp < 1.f) {
+    if (k > 0 && k < V) {
+      uint32_t t = 0;
+      for (int bit = KEY_BITS - 1; bit >= 0; --bit) {
+        const uint32_t cand = t | (1u << bit);
+        float c = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) c += key[e] >= cand ? 1.f : 0.f;
+        if (cluster_reduce(c, 0, sm, pass) >= (float)k) t = cand;
+      }
+      cut = max(cut, t);
+    }
+    const float p = a.top_p ? a.top_p[b] : 1.f;
+    if (p < 1.f) {
       float zk = z;
       if (cut > 1) {
         float s = 0.f;
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) s += key[e] >= cut ? p[e] : 0.f;
+        for (int e = 0; e < EPT; ++e) s += key[e] >= cut ? __expf(x[e] - mx) : 0.f;
         zk = cluster_reduce(s, 0, sm, pass);
       }
-      // below the top-k floor every probe passes (the mass there is at least zk)
-      cut = max(cut, search_cut<EPT, KEY_BITS, true, 2>(key, p, tp * zk, cut, sm.vec_part, sm.vec_slot, pass));
+      const float target = p * zk;
+      uint32_t t = 0;
+      for (int bit = KEY_BITS - 1; bit >= 0; --bit) {
+        const uint32_t cand = t | (1u << bit);
+        if (cand < cut) {  // below the top-k floor every probe passes
+          t = cand;
+          continue;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) s += key[e] >= cand ? __expf(x[e] - mx) : 0.f;
+        if (cluster_reduce(s, 0, sm, pass) >= target) t = cand;
+      }
+      cut = max(cut, t);
     }
   }
 
@@ -277,11 +223,9 @@ __global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel
   for (int e = 0; e < EPT; ++e) {
     const int li = e * SNT + (int)threadIdx.x;
     const int i = base + li;
-    // (the scaled logit is re-read here rather than kept live through the cut-off search)
-    const float xe = key[e] != 0u ? ld_logit<T>(row, i) * inv_t : -INFINITY;
-    bool keep = key[e] != 0u && (greedy && KEY_BITS == 32 ? xe == mx : key[e] >= cut);
+    bool keep = key[e] != 0u && (greedy && KEY_BITS == 32 ? x[e] == mx : key[e] >= cut);
     if (keep) {
-      float score = xe - mx;
+      float score = x[e] - mx;
       if (!greedy) {
         uint32_t c[4] = {(uint32_t)i, (uint32_t)(a.row0 + b), (uint32_t)off, (uint32_t)(off >> 32)};
         philox4x32_10(c, seed_lo, seed_hi);
