@@ -23,6 +23,8 @@ class GGMLType(enum.IntEnum):
     Q5_K = 13
     Q6_K = 14
     Q8_K = 15
+    IQ4_NL = 20
+    IQ4_XS = 23
     I8 = 24
     I16 = 25
     I32 = 26
@@ -38,6 +40,7 @@ BLOCK_SIZES = {
     GGMLType.Q8_0: (32, 34), GGMLType.Q8_1: (32, 36),
     GGMLType.Q2_K: (256, 84), GGMLType.Q3_K: (256, 110), GGMLType.Q4_K: (256, 144), GGMLType.Q5_K: (256, 176),
     GGMLType.Q6_K: (256, 210), GGMLType.Q8_K: (256, 292),
+    GGMLType.IQ4_NL: (32, 18), GGMLType.IQ4_XS: (256, 136),
     GGMLType.I8: (1, 1), GGMLType.I16: (1, 2), GGMLType.I32: (1, 4), GGMLType.I64: (1, 8), GGMLType.F64: (1, 8),
 }
 
@@ -47,3 +50,4 @@ KV_UINT8, KV_INT8, KV_UINT16, KV_INT16, KV_UINT32, KV_INT32, KV_FLOAT32, KV_BOOL
 
 GGUF_MAGIC = 0x46554747
 GGUF_VERSION = 3
+

@@ -99,6 +99,17 @@ def dequantize_q4_k(raw, n):
     return out.reshape(-1)
 
 
+def _extra():
+    from . import kquants as k
+    return {GGMLType.Q5_0: k.dequantize_q5_0, GGMLType.Q5_1: k.dequantize_q5_1, GGMLType.Q8_1: k.dequantize_q8_1,
+            GGMLType.Q2_K: k.dequantize_q2_k, GGMLType.Q3_K: k.dequantize_q3_k, GGMLType.Q5_K: k.dequantize_q5_k,
+            GGMLType.Q6_K: k.dequantize_q6_k, GGMLType.Q8_K: k.dequantize_q8_k,
+            GGMLType.IQ4_NL: k.dequantize_iq4_nl, GGMLType.IQ4_XS: k.dequantize_iq4_xs}
+
+
+_EXTRA = _extra()
+
+
 def dequantize(raw: np.ndarray, typ: int, n: int) -> np.ndarray:
     typ = GGMLType(typ)
     if typ == GGMLType.F32:
@@ -118,6 +129,8 @@ def dequantize(raw: np.ndarray, typ: int, n: int) -> np.ndarray:
         return dequantize_q4_k(raw, n)
     if typ == GGMLType.I8:
         return np.asarray(raw).view(np.int8)[:n].astype(np.float32)
+    if typ in _EXTRA:
+        return _EXTRA[typ](raw, n)
     raise NotImplementedError(f"dequantisation of {typ.name} is not implemented")
 
 

@@ -78,7 +78,10 @@ class GGUFReader:
         E = self.get("expert_count")
         if E:
             moe = MoEConfig(num_experts=int(E), top_k=int(self.get("expert_used_count", 2)),
-                            expert_ffn=int(self.get("expert_feed_forward_length", self.get("feed_forward_length"))))
+                            expert_ffn=int(self.get("expert_feed_forward_length", self.get("feed_forward_length"))),
+                            num_shared_experts=int(self.get("expert_shared_count", 0)),
+                            num_zero_experts=int(self.get("expert_zero_count", 0)),
+                            ffn_prefix_layers=int(self.get("moe_dense_prefix", 0)))
         dsa = DSAConfig(enabled=bool(self.get("dsa.enabled", False)))
         if dsa.enabled:
             dsa.indexer_heads = int(self.get("dsa.indexer_heads", 4))

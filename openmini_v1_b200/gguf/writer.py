@@ -82,6 +82,8 @@ class GGUFWriter:
             data = quants.quantize_q8_0(a).tobytes()
         elif typ == GGMLType.I8:
             data = a.astype(np.int8).tobytes()
+        elif typ in _KQ:
+            data = _KQ[typ](a).tobytes()
         else:
             raise NotImplementedError(typ)
         self.tensors.append((name, dims, int(typ), data))
@@ -110,3 +112,12 @@ class GGUFWriter:
             for (name, dims, typ, data), o in zip(self.tensors, offsets):
                 f.write(data)
                 f.write(b"\0" * ((-len(data)) % self.alignment))
+
+
+def _kq():
+    from . import kquants as k
+    return {GGMLType.Q5_0: k.quantize_q5_0, GGMLType.Q5_1: k.quantize_q5_1, GGMLType.Q6_K: k.quantize_q6_k,
+            GGMLType.Q8_K: k.quantize_q8_k, GGMLType.IQ4_NL: k.quantize_iq4_nl}
+
+
+_KQ = _kq()

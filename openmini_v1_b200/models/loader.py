@@ -143,7 +143,9 @@ def load_gguf_model(path: str, device="cpu", par=None, weight_format="bf16", dty
         o = src.get("blk.{i}.attn_output.weight", i)
         L["o"] = _load_linear(src, o, model, col_slice=(r * model.hq * hd, (r + 1) * model.hq * hd))
         if src.find("blk.{i}.ffn_gate_inp.weight", i) is not None:
-            raise NotImplementedError("MoE GGUF checkpoints: use the random-init MoE preset")
+            _load_moe(src, model, L, i)
+            model.layers.append(L)
+            continue
         F = model.ffn
         g = src.get("blk.{i}.ffn_gate.weight", i).to_numpy()[r * F:(r + 1) * F]
         u = src.get("blk.{i}.ffn_up.weight", i).to_numpy()[r * F:(r + 1) * F]
@@ -151,6 +153,29 @@ def load_gguf_model(path: str, device="cpu", par=None, weight_format="bf16", dty
         L["down"] = _load_linear(src, src.get("blk.{i}.ffn_down.weight", i), model, col_slice=(r * F, (r + 1) * F))
         model.layers.append(L)
     return model
+
+
+def _load_moe(src: _Src, model: DecoderLM, L: dict, i: int):
+    """MoE FFN of layer i from llama.cpp's stacked expert tensors: ffn_gate_inp [E(+Z), D],
+    ffn_{gate,up}_exps [E, Fe, D], ffn_down_exps [E, D, Fe] and the optional shared expert
+    ffn_{gate,up}_shexp [Fs, D], ffn_down_shexp [D, Fs] (column / row split under TP).
+    Reference: the MoE layer weights of openmini-server/src/model/inference/model.rs:813-960."""
+    L["router"] = torch.from_numpy(np.ascontiguousarray(src.get("blk.{i}.ffn_gate_inp.weight", i).to_numpy())) \
+        .to(model.dtype).to(model.device)
+    g = src.get("blk.{i}.ffn_gate_exps.weight", i).to_numpy()
+    u = src.get("blk.{i}.ffn_up_exps.weight", i).to_numpy()
+    d = src.get("blk.{i}.ffn_down_exps.weight", i).to_numpy()
+    L["experts_gate_up"] = [_wrap(model, torch.from_numpy(np.concatenate([g[e], u[e]]))) for e in range(g.shape[0])]
+    L["experts_down"] = [_wrap(model, torch.from_numpy(np.ascontiguousarray(d[e]))) for e in range(d.shape[0])]
+    if src.find("blk.{i}.ffn_gate_shexp.weight", i) is not None:
+        tp, r = model.par.tp, model.par.tp_rank
+        sg = src.get("blk.{i}.ffn_gate_shexp.weight", i).to_numpy()
+        su = src.get("blk.{i}.ffn_up_shexp.weight", i).to_numpy()
+        sd = src.get("blk.{i}.ffn_down_shexp.weight", i).to_numpy()
+        Fs = sg.shape[0] // tp
+        L["shared_gate_up"] = _wrap(model, torch.from_numpy(np.concatenate([sg[r * Fs:(r + 1) * Fs],
+                                                                            su[r * Fs:(r + 1) * Fs]])))
+        L["shared_down"] = _wrap(model, torch.from_numpy(np.ascontiguousarray(sd[:, r * Fs:(r + 1) * Fs])))
 
 
 def _wrap(model, w: torch.Tensor):
@@ -163,7 +188,7 @@ def _wrap(model, w: torch.Tensor):
 
 
 def save_gguf_model(model: DecoderLM, path: str, quant: str = "f32", tokenizer_tokens=None):
-    """Write an unsharded DecoderLM (tp = 1) as GGUF. quant: f32 | f16 | bf16 | q4_0 | q8_0 | i8."""
+    """Write an unsharded DecoderLM (tp = 1) as GGUF. quant: f32 | f16 | bf16 | q4_0 | q8_0 | i8 | q6_k | q5_0 | q8_k | iq4_nl."""
     cfg = model.cfg
     if model.par.tp != 1:
         raise ValueError("save an unsharded (tp=1) model")
@@ -175,11 +200,19 @@ def save_gguf_model(model: DecoderLM, path: str, quant: str = "f32", tokenizer_t
                  ("rope.freq_base", float(cfg.rope_theta)), ("attention.layer_norm_rms_epsilon", float(cfg.rms_eps)),
                  ("vocab_size", cfg.vocab_size)]:
         w.add_kv(a + k, v)
+    if cfg.moe.num_experts:
+        w.add_kv(a + "expert_count", cfg.moe.num_experts)
+        w.add_kv(a + "expert_used_count", cfg.moe.top_k)
+        w.add_kv(a + "expert_feed_forward_length", cfg.moe.expert_ffn)
+        w.add_kv(a + "expert_shared_count", cfg.moe.num_shared_experts)
+        w.add_kv(a + "expert_zero_count", cfg.moe.num_zero_experts)
+        w.add_kv(a + "moe_dense_prefix", cfg.moe.ffn_prefix_layers)
     w.add_kv("general.name", cfg.name)
     if tokenizer_tokens:
         w.add_kv("tokenizer.ggml.tokens", list(tokenizer_tokens))
     typ = {"f32": GGMLType.F32, "f16": GGMLType.F16, "bf16": GGMLType.BF16, "q4_0": GGMLType.Q4_0,
-           "q8_0": GGMLType.Q8_0, "i8": GGMLType.I8}[quant]
+           "q8_0": GGMLType.Q8_0, "i8": GGMLType.I8, "q6_k": GGMLType.Q6_K, "q5_0": GGMLType.Q5_0,
+           "q8_k": GGMLType.Q8_K, "iq4_nl": GGMLType.IQ4_NL}[quant]
 
     def npf(t):
         if not isinstance(t, torch.Tensor):
@@ -208,6 +241,20 @@ def save_gguf_model(model: DecoderLM, path: str, quant: str = "f32", tokenizer_t
         add_lin(f"blk.{i}.attn_k.weight", qkv[nq:nq + nk])
         add_lin(f"blk.{i}.attn_v.weight", qkv[nq + nk:])
         add_lin(f"blk.{i}.attn_output.weight", npf(L["o"]))
+        if "router" in L:
+            w.add_tensor(f"blk.{i}.ffn_gate_inp.weight", npf(L["router"]))
+            gus = np.stack([npf(t) for t in L["experts_gate_up"]])
+            Fe = gus.shape[1] // 2
+            add_lin(f"blk.{i}.ffn_gate_exps.weight", gus[:, :Fe])
+            add_lin(f"blk.{i}.ffn_up_exps.weight", gus[:, Fe:])
+            add_lin(f"blk.{i}.ffn_down_exps.weight", np.stack([npf(t) for t in L["experts_down"]]))
+            if "shared_gate_up" in L:
+                sgu = npf(L["shared_gate_up"])
+                Fs = sgu.shape[0] // 2
+                add_lin(f"blk.{i}.ffn_gate_shexp.weight", sgu[:Fs])
+                add_lin(f"blk.{i}.ffn_up_shexp.weight", sgu[Fs:])
+                add_lin(f"blk.{i}.ffn_down_shexp.weight", npf(L["shared_down"]))
+            continue
         gu = npf(L["gate_up"])
         F = cfg.intermediate_size
         add_lin(f"blk.{i}.ffn_gate.weight", gu[:F])
