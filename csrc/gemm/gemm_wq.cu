@@ -63,7 +63,7 @@ static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g
 //   (qtype 0, Q4: 4608-byte tiles = 128 rows x 32 B nibbles + [2][128] bf16 scales;
 //    qtype 1, INT8: 8192-byte tiles = 128 rows x 64 offset-binary bytes);
 // scales: INT8 only, fp32 [N] per-row scale (applied in the epilogue).
-// Decode (M <= 128 tokens, with a workspace and the zeroed counters `sem`) runs the
+// Decode (M <= 256 tokens, with a workspace and the zeroed counters `sem`) runs the
 // stream-K TMEM-operand kernel (gemm_wq_dec.cuh); larger M and prefill run the
 // shared-memory-operand kernel (gemm_wq.cuh) with split-K planned by a byte model.
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
@@ -120,19 +120,22 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
 
   // ---------------------------------------------------------------- stream-K decode kernel
   const int dec_ch = qtype == 0 ? 4 : 2;
-  const int dec_r = bx == 32 ? 2 : 1;  // = WqDecCfg<bx, *>::R
-  if (swap && bx <= 128 && force_splits <= 0 && sem.has_value() && ws && g.num_kb % dec_ch == 0) {
-    const int groups = (wt_tiles + dec_r - 1) / dec_r;
+  const int dec_bx = std::min(bx, 128);
+  const int dec_nh = (M + dec_bx - 1) / dec_bx;  // token halves (2 for 128 < M <= 256)
+  const int dec_r = dec_bx == 32 ? 2 : 1;        // = WqDecCfg<dec_bx, *>::R
+  if (swap && force_splits <= 0 && sem.has_value() && ws && g.num_kb % dec_ch == 0) {
+    const int groups = (wt_tiles + dec_r - 1) / dec_r * dec_nh;
     const int nc = g.num_kb / dec_ch;
     const long long total = (long long)groups * nc;
     const int grid = (int)std::min<long long>(sms, total);
-    const size_t part_bytes = (size_t)grid * 2 * dec_r * 128 * bx * sizeof(float);
+    const size_t part_bytes = (size_t)grid * 2 * dec_r * 128 * dec_bx * sizeof(float);
     TORCH_CHECK(part_bytes <= ws_bytes, "gemm_wq: workspace too small for the decode partials");
     TORCH_CHECK(sem->is_cuda() && sem->scalar_type() == at::kInt && sem->is_contiguous() && sem->numel() >= groups,
                 "gemm_wq: sem must be zeroed int32 with one counter per row group");
     g.rgroup = dec_r;
     g.sk_total = total;
     g.sk_nc = nc;
+    g.sk_nh = dec_nh;
     g.part = ws;
     g.sem = sem->data_ptr<int>();
     g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
@@ -150,11 +153,11 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     }
     // activations as [K/64][M][64]: a box {64, bx, ch} is `ch` swizzled [bx][64] tiles
     CUtensorMap tx = om::make_tmap_3d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, K / 64, x.stride(0),
-                                      64, 64, bx, dec_ch, CU_TENSOR_MAP_SWIZZLE_128B);
+                                      64, 64, dec_bx, dec_ch, CU_TENSOR_MAP_SWIZZLE_128B);
     if (qtype == 0)
-      om::dispatch_dec<om::WQ_Q4>(bx, tx, g, grid, st);
+      om::dispatch_dec<om::WQ_Q4>(dec_bx, tx, g, grid, st);
     else
-      om::dispatch_dec<om::WQ_I8>(bx, tx, g, grid, st);
+      om::dispatch_dec<om::WQ_I8>(dec_bx, tx, g, grid, st);
     return;
   }
 

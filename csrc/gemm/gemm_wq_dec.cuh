@@ -24,6 +24,15 @@
 // applies the final epilogue (per-row INT8 scale, residual, peer-output stores).
 // No CTA ever waits for another one.
 //
+// Token halves: for 128 < M <= 256 the 128-token kernel runs every row group twice,
+// once per half of the tokens (item group = row group * 2 + half), so a weight chunk
+// is re-read from L2 right after its first use and the MMA stays 128 x 128.
+//
+// Fix-up of the CTA's last segment: when the CTA that completes a group does so in
+// its final segment, nothing is left to overlap the fix-up with, so every warp of
+// the CTA sums the slots (float4 over four weight rows, one token row of 512 bytes
+// per warp and slot), instead of only the four epilogue warps.
+//
 // Handshakes are per raw chunk (CH K blocks = 16 MMAs of K = 16), not per K block:
 // one issuing thread runs every MMA of the SM, and each wait / fence / commit it
 // executes costs about as much as four MMAs, so a per-K-block handshake capped the
@@ -141,6 +150,76 @@ __device__ __forceinline__ void dec_store_rows(const GemmArgs& g, const float (&
   }
 }
 
+// Final epilogue of four weight rows rr..rr+3 of token tok (values already summed, the
+// INT8 per-row scales applied by the caller).
+__device__ __forceinline__ void dec_store4(const GemmArgs& g, int tok, int rr, float4 v) {
+  __nv_bfloat16* dst = out_row(g, g.out, tok) + rr;
+  const __nv_bfloat16* rs = g.epi == EPI_RESID ? g.resid + (size_t)tok * g.ldo + rr : nullptr;
+  if (g.vec_out && rr + 4 <= g.rows) {
+    if (rs) {
+      const uint2 r2 = *reinterpret_cast<const uint2*>(rs);
+      v.x += bf16lo(r2.x); v.y += bf16hi(r2.x); v.z += bf16lo(r2.y); v.w += bf16hi(r2.y);
+    }
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  } else {
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    for (int q = 0; q < 4 && rr + q < g.rows; ++q)
+      dst[q] = __float2bfloat16_rn(rs ? f[q] + __bfloat162float(rs[q]) : f[q]);
+  }
+}
+
+// Sum of item group gg's fp32 slots (contributing CTAs c_lo..c_hi, in CTA order, so the
+// result does not depend on which CTA finishes) and the final epilogue, by threads
+// tid < nth (a multiple of 32): lane = four weight rows, warps stride over the tokens,
+// U tokens per thread in flight per slot.
+template <int BX, int R, int U>
+__device__ void dec_fixup(const GemmArgs& g, long long gg, int grp, int half, int nR, int c_lo, int c_hi,
+                          int tid, int nth) {
+  const int NC = g.sk_nc;
+  const long long T = g.sk_total, P = gridDim.x;
+  const size_t slot_floats = (size_t)R * BX * 128;
+  const int lane = tid & 31, w = tid >> 5, nw = nth >> 5;
+  const int tok0 = half * BX;
+  const int ntok = min(BX, g.cols - tok0);
+  for (int j = 0; j < nR; ++j) {
+    const int rr = (grp * R + j) * 128 + 4 * lane;
+    float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (g.wscale) {
+      sc.x = rr < g.rows ? g.wscale[rr] : 1.f;
+      sc.y = rr + 1 < g.rows ? g.wscale[rr + 1] : 1.f;
+      sc.z = rr + 2 < g.rows ? g.wscale[rr + 2] : 1.f;
+      sc.w = rr + 3 < g.rows ? g.wscale[rr + 3] : 1.f;
+    }
+    for (int t0 = w; t0 < ntok; t0 += nw * U) {
+      float4 acc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c2 = c_lo; c2 <= c_hi; ++c2) {
+        const long long b2 = (long long)c2 * T / P;
+        const int sl = b2 / NC == gg ? 0 : 1;
+        const float* src = g.part + ((size_t)c2 * 2 + sl) * slot_floats + (size_t)j * BX * 128 + 4 * lane;
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int t = t0 + u * nw;
+          v[u] = t < ntok ? __ldcg(reinterpret_cast<const float4*>(src + (size_t)t * 128)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int t = t0 + u * nw;
+        if (t >= ntok || rr >= g.rows) continue;
+        const float4 o = make_float4(acc[u].x * sc.x, acc[u].y * sc.y, acc[u].z * sc.z, acc[u].w * sc.w);
+        dec_store4(g, tok0 + t, rr, o);
+      }
+    }
+  }
+}
+
 // A CTA's item range [ib, ie) in processing order: the partial head segment (items
 // of the range's first group), then the partial tail segment (its last group), then
 // the full groups in between. The two partial segments are the ones whose fp32 slots
@@ -181,10 +260,12 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   __shared__ int s_last;
+  __shared__ long long s_fix[4];  // deferred fix-up of the final segment: gg, c_lo, c_hi, nR (gg < 0: none)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int NC = g.sk_nc;
+  const int NH = g.sk_nh;
   const long long T = g.sk_total;
   const long long P = gridDim.x;
   const long long ib = (long long)blockIdx.x * T / P;
@@ -209,6 +290,7 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
     }
+    s_fix[0] = -1;
     fence_barrier_init();
   }
   if (warp == 3 && lane == 0) tma_prefetch_desc(&tmX);
@@ -224,7 +306,7 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
       bool ok = true;
       for (long long k = 0; k < nk && ok; ++k) {
         const long long i = ord.at(k);
-        const int grp = (int)(i / NC), ch = (int)(i % NC);
+        const int grp = (int)(i / NC / NH), ch = (int)(i % NC);
         const int nR = min(R, g.wt_tiles - grp * R);
         for (int j = 0; j < nR; ++j, ++t) {
           const int s = t % RS;
@@ -243,11 +325,12 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
       int ix = 0;
       bool ok = true;
       for (long long k = 0; k < nk; ++k, ++ix) {
-        const int ch = (int)(ord.at(k) % NC);
+        const long long i = ord.at(k);
+        const int ch = (int)(i % NC), half = (int)(i / NC % NH);
         const int s = ix % XS;
         if (!mbar_wait(&x_empty[s], ((ix / XS) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
         mbar_arrive_expect_tx(&x_full[s], C::XSLOT);
-        tma_load_3d(xbuf + s * C::XSLOT, &tmX, &x_full[s], 0, 0, ch * CH);
+        tma_load_3d(xbuf + s * C::XSLOT, &tmX, &x_full[s], 0, half * BX, ch * CH);
       }
       if (!ok)
         for (int q = max(0, ix - XS); q < ix; ++q) mbar_wait(&x_full[q % XS], (q / XS) & 1, nullptr, 0);
@@ -260,7 +343,7 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
       bool ok = true;
       for (long long k = 0; k < nk && ok; ++k, ++ix) {
         const long long i = ord.at(k);
-        const int grp = (int)(i / NC), ch = (int)(i % NC);
+        const int grp = (int)(i / NC / NH), ch = (int)(i % NC);
         const bool first = k == 0 || ch == 0 || ord.at(k - 1) != i - 1;
         const bool last = k == nk - 1 || ch == NC - 1 || ord.at(k + 1) != i + 1;
         const int nR = min(R, g.wt_tiles - grp * R);
@@ -306,16 +389,15 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
     int t = 0;
     bool ok = true;
     for (long long k = 0; k < nk && ok; ++k) {
-      const int grp = (int)(ord.at(k) / NC);
+      const int grp = (int)(ord.at(k) / NC / NH);
       const int nR = min(R, g.wt_tiles - grp * R);
       for (int j = 0; j < nR; ++j, ++t) {
         if (t % NG != grp_id) continue;
         const int s = t % RS;
         if (!mbar_wait(&raw_full[s], (t / RS) & 1, g.status, OM_ERR_WAIT_FULL)) { ok = false; break; }
         const uint32_t slot = raw_s + s * C::SLOT;
-        // Stage the thread's whole row of the chunk in registers and release the raw
-        // slot at once: a bulk copy takes ~4 us to land under full HBM load, so every
-        // microsecond a slot stays held is bandwidth lost (slots / (latency + hold)).
+        // Stage the thread's whole row of the chunk in registers (the slot is released
+        // after the tensor-memory stores below, behind a generic -> async proxy fence).
         constexpr int WPK = QT == WQ_Q4 ? 8 : 16;  // packed 32-bit words per row per K block
         uint32_t wr[CH][WPK];
         uint32_t sc[CH];  // Q4: the row's two bf16 block scales of each K block
@@ -330,8 +412,7 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
           if (QT == WQ_Q4)
             sc[kk] = lds_u16(base + C::RAW_Q + row * 2) | (lds_u16(base + C::RAW_Q + 256 + row * 2) << 16);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[s]);
+
         // the group's A slots are free once the MMA finished this group's previous chunk
         if (!mbar_wait(&a_empty[grp_id], ((t / NG) & 1) ^ 1, g.status, OM_ERR_WAIT_EMPTY)) { ok = false; break; }
         tc_fence_after();
@@ -363,6 +444,12 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[grp_id]);
+        // Release the raw slot only now, behind a proxy fence: the next bulk copy into it
+        // is an async-proxy write, and without the fence it overwrote rows that the generic
+        // loads above had not yet read (measured: INT8 outputs differed from run to run).
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[s]);
         if (!ok) break;
       }
     }
@@ -376,7 +463,9 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
     int seg = 0, seg_ch0 = 0;
     for (long long k = 0; k < nk; ++k) {
       const long long i = ord.at(k);
-      const int grp = (int)(i / NC), ch = (int)(i % NC);
+      const long long gg = i / NC;
+      const int grp = (int)(gg / NH), half = (int)(gg % NH), ch = (int)(i % NC);
+      const int tok0 = half * BX;
       if (k == 0 || ch == 0 || ord.at(k - 1) != i - 1) seg_ch0 = ch;
       if (!(k == nk - 1 || ch == NC - 1 || ord.at(k + 1) != i + 1)) continue;
       const int nR = min(R, g.wt_tiles - grp * R);
@@ -384,7 +473,7 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
       if (!mbar_wait(&tfull[acc], (seg >> 1) & 1, g.status, OM_ERR_WAIT_ACCUM)) break;
       tc_fence_after();
       const bool full = seg_ch0 == 0 && ch == NC - 1;
-      const int slot = grp == (int)(ib / NC) ? 0 : 1;  // the range's first group: slot 0
+      const int slot = gg == ib / NC ? 0 : 1;  // the range's first item group: slot 0
       float* mine = g.part + ((size_t)blockIdx.x * 2 + slot) * slot_floats;
       for (int j = 0; j < nR; ++j) {
         const int r = (grp * R + j) * 128 + rl;
@@ -394,12 +483,12 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tb + cc * 32, v);
           tc_wait_ld();
-          if (cc * 32 >= g.cols) continue;
+          if (tok0 + cc * 32 >= g.cols) continue;
           float f[32];
 #pragma unroll
           for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
           if (full) {
-            dec_store_rows(g, f, r - lane, cc * 32, stage, g.epi, g.out, g.resid, vec_out);
+            dec_store_rows(g, f, r - lane, tok0 + cc * 32, stage, g.epi, g.out, g.resid, vec_out);
           } else {
             float* dst = mine + (size_t)(j * BX + cc * 32) * 128 + rl;
 #pragma unroll
@@ -413,34 +502,26 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
         // counter protocol: the CTA that completes the group's last segment finishes it
         __threadfence();
         named_bar_sync(1, 128);
-        const long long g0 = (long long)grp * NC, g1 = g0 + NC - 1;
+        const long long g0 = gg * NC, g1 = g0 + NC - 1;
         const int c_lo = (int)(((g0 + 1) * P + T - 1) / T - 1);
         const int c_hi = (int)(((g1 + 1) * P + T - 1) / T - 1);
         if (rl == 0) {
-          const int prev = atomicAdd(&g.sem[grp], 1);
+          const int prev = atomicAdd(&g.sem[gg], 1);
           s_last = prev == c_hi - c_lo;
-          if (s_last) g.sem[grp] = 0;  // zero again for the next launch
+          if (s_last) g.sem[gg] = 0;  // zero again for the next launch
         }
         named_bar_sync(1, 128);
         if (s_last) {
           __threadfence();
-          for (int j = 0; j < nR; ++j) {
-            const int r = (grp * R + j) * 128 + rl;
-#pragma unroll 1
-            for (int cc = 0; cc < BX / 32; ++cc) {
-              if (cc * 32 >= g.cols) continue;
-              float f[32];
-#pragma unroll
-              for (int q = 0; q < 32; ++q) f[q] = 0.f;
-              for (int c2 = c_lo; c2 <= c_hi; ++c2) {
-                const long long b2 = (long long)c2 * T / P;
-                const int sl = (int)(b2 / NC) == grp ? 0 : 1;
-                const float* src = g.part + ((size_t)c2 * 2 + sl) * slot_floats + (size_t)(j * BX + cc * 32) * 128 + rl;
-#pragma unroll
-                for (int q = 0; q < 32; ++q) f[q] += __ldcg(src + q * 128);
-              }
-              dec_store_rows(g, f, r - lane, cc * 32, stage, g.epi, g.out, g.resid, vec_out);
+          if (k == nk - 1) {  // nothing left to overlap with: the whole CTA sums after the loop
+            if (rl == 0) {
+              s_fix[0] = gg;
+              s_fix[1] = c_lo;
+              s_fix[2] = c_hi;
+              s_fix[3] = nR;
             }
+          } else {
+            dec_fixup<BX, R, 8>(g, gg, grp, half, nR, c_lo, c_hi, rl, 128);
           }
         }
       }
@@ -448,6 +529,13 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
     }
   }
 
+  __syncthreads();
+  if (s_fix[0] >= 0) {
+    __threadfence();
+    const long long gg = s_fix[0];
+    dec_fixup<BX, R, 4>(g, gg, (int)(gg / NH), (int)(gg % NH), (int)s_fix[3], (int)s_fix[1], (int)s_fix[2],
+                        threadIdx.x, C::THREADS);
+  }
   if (g.po.pworld > 0) __threadfence_system();  // peer-output stores of this thread
   __syncthreads();
   peer_publish(g.po);

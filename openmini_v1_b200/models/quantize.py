@@ -211,7 +211,7 @@ def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     c = ops.ctx(x.device)
     ws = c.workspace("gemm", ops.GEMM_WS_FLOATS)
     r2 = resid.reshape(-1, N) if resid is not None else None
-    # decode (M <= 128) runs the stream-K kernel: its per-group counters are ``sem``
+    # decode (M <= 256) runs the stream-K kernel: its per-group counters are ``sem``
     kw = {"sem": c.semaphores()}
     if peer is not None:
         kw["peer"] = peer
