@@ -49,8 +49,13 @@ def _args():
     p.add_argument("--out-tokens", type=int, default=512)
     p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; not the metric)")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--tp-transport", default="symm", choices=["symm", "nccl"],
-                   help="symm: fused reduce/RMSNorm/all-gather over peer memory; nccl: all-reduce baseline")
+    p.add_argument("--trace", type=int, default=0,
+                   help="after the timed run, profile this many extra device decode steps and print the "
+                        "per-kernel device-time table of every rank to stderr (not part of the metric)")
+    p.add_argument("--tp-transport", default="symm", choices=["symm", "symm_push", "nccl"],
+                   help="symm: fused reduce/RMSNorm/all-gather over peer memory (partials pulled by the "
+                        "reduce kernel); symm_push: the row-parallel GEMM stores its partials into the "
+                        "owners' buffers; nccl: all-reduce baseline")
     return p.parse_args()
 
 
@@ -245,6 +250,26 @@ def main():
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if a.trace > 0:
+        from openmini_v1_b200.utils.trace import by_position, format_table, kernel_sequence, kernel_table
+        ht = eng.begin_multi_decode(a.trace + 2)  # one warm step, the table, one ordered step
+        eng.multi_decode_step(ht)
+        barrier()
+        rows, total = kernel_table(lambda: eng.multi_decode_step(ht), iters=a.trace)
+        seq = kernel_sequence(lambda: eng.multi_decode_step(ht))
+        eng.finish_multi_decode(ht)
+        gemm = [r for r in rows if "gemm_wq" in r[0] or "gemm_bf16" in r[0]]
+        pos = by_position(seq, gemm[0][0], 4) if gemm else []
+        table = format_table(rows, total, per=a.trace,
+                             title=f"rank {rank}/{world}: {a.trace} profiled decode steps (shares, not timings)")
+        for r in range(world):
+            if world > 1:
+                dist.barrier()
+            if r == rank:
+                print(table, file=sys.stderr, flush=True)
+                if pos:
+                    print("top GEMM by position in the layer (qkv, o, gate_up, down): "
+                          + ", ".join(f"{p}: {us:.1f} us x{n}" for p, n, us in pos), file=sys.stderr, flush=True)
     if world > 1:
         # Captured decode graphs hold NCCL work; tearing the communicator down
         # under them can block, so ranks leave together after a final barrier.

@@ -8,7 +8,7 @@ std::vector<int64_t> om_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, 
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
                 torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer,
-                c10::optional<torch::Tensor> sem);
+                c10::optional<torch::Tensor> sem, std::vector<int64_t> agwait);
 void om_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w, torch::Tensor out,
                 double eps);
 void om_layernorm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, torch::Tensor out,
@@ -61,7 +61,8 @@ void om_symm_close(int64_t ptr);
 torch::Tensor om_symm_view(int64_t ptr, int64_t offset, std::vector<int64_t> shape, int64_t dtype_code);
 void om_sp_signal(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::Tensor h, torch::Tensor w,
-                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push);
+                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push,
+                              bool signal);
 void om_sp_wait(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
 
 void om_moe_route(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> forced, torch::Tensor ids,
@@ -82,7 +83,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("x"), py::arg("qtiles"), py::arg("scales"), py::arg("qtype"), py::arg("out"),
         py::arg("resid") = py::none(), py::arg("workspace") = py::none(), py::arg("status"),
         py::arg("force_swap") = -1, py::arg("force_splits") = 0, py::arg("peer") = std::vector<int64_t>{},
-        py::arg("sem") = py::none());
+        py::arg("sem") = py::none(), py::arg("agwait") = std::vector<int64_t>{});
   m.def("rmsnorm", &om_rmsnorm, py::arg("x"), py::arg("delta"), py::arg("w"), py::arg("out"), py::arg("eps"));
   m.def("layernorm", &om_layernorm);
   m.def("silu_mul", &om_silu_mul);
@@ -125,6 +126,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sp_reduce_norm_gather", &om_sp_reduce_norm_gather,
         "sum peer partials into own residual rows, RMSNorm, push normed rows to every rank",
         py::arg("bases"), py::arg("rank"), py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("p_off"),
-        py::arg("x_off"), py::arg("status"), py::arg("push") = false);
+        py::arg("x_off"), py::arg("status"), py::arg("push") = false, py::arg("signal") = false);
   m.def("sp_wait", &om_sp_wait, "wait until every rank pushed its normed rows for this epoch");
 }

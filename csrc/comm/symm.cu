@@ -23,7 +23,11 @@
 //               gather region (all-gather by push); the last CTA then bumps
 //               agdone[me] on every peer
 //   sp_wait     wait agdone[p] >= epoch for all p (the gathered activations are
-//               complete); the next column-parallel GEMM reads them locally
+//               complete); the next column-parallel GEMM reads them locally. A weight-only
+//               decode GEMM does this wait itself (GemmArgs::agwait, in its activation
+//               producer warp), so its weight stream starts before the gather completes.
+// Pull mode (the default) folds sp_signal into sp_reduce (SpArgs::signal): block 0
+// publishes ready[me] at the start and the last CTA stores the new epoch.
 // so reduce-scatter, residual add, RMSNorm and all-gather are one kernel and
 // each byte crosses NVLink once.
 //
@@ -58,6 +62,9 @@ struct SpArgs {
   long long x_off;              // gathered normed-activation region offset
   int push;                     // 1: the partials were pushed into this rank's slots by the
                                 // peer-output GEMM ([world][rows_own][D] at p_off, local reads)
+  int signal;                   // 1: this kernel opens the epoch (epoch + 1) and block 0 publishes
+                                // ready[rank] on every peer first (pull mode: the partials were
+                                // written locally by the previous kernel)
   __nv_bfloat16* h;             // own residual rows [rows_own, D]
   const __nv_bfloat16* w;       // RMSNorm weight [D]
   float eps;
@@ -109,7 +116,18 @@ template <int NT>
 __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const __grid_constant__ SpArgs a) {
   __shared__ float red[NT / 32];
   __shared__ int go;
-  const int e = *ctrl(a.base[a.rank], 128);
+  // epoch of this event: pushed partials -> the GEMM already advanced it; signal mode ->
+  // every CTA reads the previous value here and the last CTA stores e at the end (after
+  // every CTA has taken its ticket, so no CTA can read the new value at its start)
+  const int e = *ctrl(a.base[a.rank], 128) + (a.signal ? 1 : 0);
+  if (a.signal && blockIdx.x == 0 && threadIdx.x == 0) {
+    // the previous kernel's partials are complete (stream order); make them visible to the
+    // peers before the flag they acquire
+    __threadfence_system();
+#pragma unroll
+    for (int p = 0; p < SP_MAX_WORLD; ++p)
+      if (p < a.world) st_release_sys(ctrl(a.base[p], 0) + a.rank, e);
+  }
   // every event waits for every rank's signal, also without partials: a rank that signalled
   // has finished reading the gather region this event overwrites (it was two events ago)
   if (threadIdx.x == 0) go = sp_wait_all(a, 0, e, OM_ERR_WAIT_FULL) ? 1 : 0;
@@ -125,16 +143,24 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const __grid_
         float v[8];
         unpack8(reinterpret_cast<const uint4*>(hr)[c], v);
         if (a.p_off >= 0) {
+          // issue every rank's load before the first add: the remote ones then overlap
+          uint4 u[SP_MAX_WORLD];
 #pragma unroll
           for (int p = 0; p < SP_MAX_WORLD; ++p) {
-            if (p >= a.world) break;
-            const uint8_t* src = a.push ? a.base[a.rank] + a.p_off + ((size_t)p * a.rows_own + r) * a.D * 2
-                                        : a.base[p] + a.p_off + g * a.D * 2;
-            const uint4 u = reinterpret_cast<const uint4*>(src)[c];
-            float d[8];
-            unpack8(u, d);
+            if (p < a.world) {
+              const uint8_t* src = a.push ? a.base[a.rank] + a.p_off + ((size_t)p * a.rows_own + r) * a.D * 2
+                                          : a.base[p] + a.p_off + g * a.D * 2;
+              u[p] = reinterpret_cast<const uint4*>(src)[c];
+            }
+          }
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] += d[t];
+          for (int p = 0; p < SP_MAX_WORLD; ++p) {
+            if (p < a.world) {
+              float d[8];
+              unpack8(u[p], d);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) v[t] += d[t];
+            }
           }
           const uint4 nu = pack8(v);
           reinterpret_cast<uint4*>(hr)[c] = nu;
@@ -174,6 +200,7 @@ __global__ void __launch_bounds__(NT) sp_reduce_norm_gather_kernel(const __grid_
     const unsigned t = atomicAdd(ticket, 1u);
     if (t == gridDim.x - 1) {
       *ticket = 0u;
+      if (a.signal) *ctrl(a.base[a.rank], 128) = e;
       __threadfence_system();
 #pragma unroll
       for (int p = 0; p < SP_MAX_WORLD; ++p)
@@ -254,7 +281,8 @@ void om_sp_signal(std::vector<int64_t> bases, int64_t rank, torch::Tensor status
 // h: own residual rows [rows_own, D] (updated in place when p_off >= 0);
 // normed rows land at x_off + global_row * D * 2 of every rank's buffer.
 void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::Tensor h, torch::Tensor w,
-                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push) {
+                              double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push,
+                              bool signal) {
   TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2, "sp_reduce: h");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.numel() == h.size(1), "sp_reduce: w");
   const int D = h.size(1);
@@ -265,8 +293,18 @@ void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::T
   a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   a.eps = eps;
   a.push = push ? 1 : 0;
+  a.signal = signal ? 1 : 0;
+  TORCH_CHECK(!(push && signal), "sp_reduce: pushed partials come with their own signal");
   const int grid = std::max<int>(1, std::min<int>(a.rows_own, 2 * om::num_sms()));
-  om::sp_reduce_norm_gather_kernel<256><<<grid, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(a);
+  // one thread per 16-byte vector of the row (up to 1024): every partial row of every peer
+  // is then requested at once, so a pulled row costs one NVLink round trip, not one per chunk
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  if (D / 8 >= 1024)
+    om::sp_reduce_norm_gather_kernel<1024><<<grid, 1024, 0, st>>>(a);
+  else if (D / 8 >= 512)
+    om::sp_reduce_norm_gather_kernel<512><<<grid, 512, 0, st>>>(a);
+  else
+    om::sp_reduce_norm_gather_kernel<256><<<grid, 256, 0, st>>>(a);
   OM_LAUNCH_CHECK();
 }
 

@@ -76,6 +76,8 @@ struct GemmArgs {
   // part = fp32 partial slots [gridDim.x][2][rgroup * 128 * cols_pad].
   long long sk_total;
   int sk_nc;
+  const int* agwait;  // sequence-parallel gather to wait for before the first activation load:
+  int agwait_n;       // this rank's symmetric control words (agdone[p] at byte 64, epoch at 128), ranks
   int sk_nh;         // token halves of BX tokens (2 when 128 < M <= 256): item group = row group * sk_nh + half
   float* part;
   int vec_out;       // output rows (and residual rows) 16-byte aligned: vector epilogue stores

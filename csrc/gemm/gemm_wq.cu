@@ -69,7 +69,7 @@ static void dispatch(int bx, bool swap, const CUtensorMap& tx, const GemmArgs& g
 void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tensor> scales, int64_t qtype,
                 torch::Tensor out, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> workspace,
                 torch::Tensor status, int64_t force_swap, int64_t force_splits, std::vector<int64_t> peer,
-                c10::optional<torch::Tensor> sem) {
+                c10::optional<torch::Tensor> sem, std::vector<int64_t> agwait) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_wq: x");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.dim() == 2, "gemm_wq: out");
   const int M = x.size(0), K = x.size(1), N = out.size(1);
@@ -136,6 +136,12 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     g.sk_total = total;
     g.sk_nc = nc;
     g.sk_nh = dec_nh;
+    if (!agwait.empty()) {
+      TORCH_CHECK(agwait.size() == 2 && agwait[0] != 0 && agwait[1] >= 1 && agwait[1] <= 8,
+                  "gemm_wq: agwait = [own symmetric buffer, ranks]");
+      g.agwait = reinterpret_cast<const int*>(agwait[0]);
+      g.agwait_n = (int)agwait[1];
+    }
     g.part = ws;
     g.sem = sem->data_ptr<int>();
     g.epi = rp ? om::EPI_RESID : om::EPI_STORE;
@@ -161,6 +167,7 @@ void om_gemm_wq(torch::Tensor x, torch::Tensor qtiles, c10::optional<torch::Tens
     return;
   }
 
+  TORCH_CHECK(agwait.empty(), "gemm_wq: agwait needs the decode kernel (M <= 256, workspace, sem)");
   // ---------------------------------------------------------------- shared-memory-operand kernel
   // Plan: choose the weight row-tiles per unit R (activation reuse, decode only) and
   // the split-K factor s by a byte-count model of the busiest SM: rounds of units x

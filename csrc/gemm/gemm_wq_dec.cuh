@@ -324,7 +324,25 @@ __global__ void __launch_bounds__(WqDecCfg<BX, QT>::THREADS, 1)
     if (elect_one()) {
       int ix = 0;
       bool ok = true;
-      for (long long k = 0; k < nk; ++k, ++ix) {
+      if (g.agwait_n > 0) {
+        // the activations are the rows every rank pushed into this rank's gather region in
+        // the previous sequence-parallel event: wait for all of them (bounded), then order
+        // those generic-proxy peer writes before this warp's TMA (async-proxy) reads
+        const int e = ld_volatile_s32(g.agwait + 32);
+        const uint64_t t0 = globaltimer();
+        for (int p = 0; p < g.agwait_n && ok; ++p) {
+          uint32_t spins = 0;
+          while (ld_acquire_sys_s32(g.agwait + 16 + p) < e) {
+            if ((++spins & 63u) == 0 && globaltimer() - t0 > OM_WAIT_LIMIT_NS) {
+              record_error(g.status, OM_ERR_WAIT_FULL);
+              ok = false;
+              break;
+            }
+          }
+        }
+        fence_proxy_async_global();
+      }
+      for (long long k = 0; k < nk && ok; ++k, ++ix) {
         const long long i = ord.at(k);
         const int ch = (int)(i % NC), half = (int)(i / NC % NH);
         const int s = ix % XS;

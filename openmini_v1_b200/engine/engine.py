@@ -30,6 +30,7 @@ from .. import _native, ops
 from ..models.llama import DecoderLM, ForwardBatch
 from .request import Request, RequestOutput, RequestStatus, SamplingParams
 from .scheduler import Scheduler
+from ..utils.trace import nvtx_range
 
 
 @dataclass
@@ -174,7 +175,12 @@ class LLMEngine:
 
     # ---------------------------------------------------------------- step
     def step(self) -> list:
-        so = self.sched.schedule()
+        with nvtx_range("engine.step"):
+            return self._step()
+
+    def _step(self) -> list:
+        with nvtx_range("schedule"):
+            so = self.sched.schedule()
         self.stats["preemptions"] += len(so.preempted)
         if so.kind == "idle":
             return []
@@ -186,11 +192,13 @@ class LLMEngine:
             from .speculative import eligible, spec_decode_step
             if all(eligible(c.req) for c in so.chunks):
                 return spec_decode_step(self, so, self.spec)
-        fb, samp, rows_req = self._build(so)
+        with nvtx_range("build"):
+            fb, samp, rows_req = self._build(so)
         want_routing = any(c.req.params.return_routing for c in so.chunks)
         if (so.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(so.chunks))
                 and not self._needs_eager_sampling(rows_req) and not want_routing):
-            tok, lp, mask = self.graphs.run(fb, samp, len(so.chunks))
+            with nvtx_range("decode_graph"):
+                tok, lp, mask = self.graphs.run(fb, samp, len(so.chunks))
         else:
             if want_routing:
                 fb.record_routing = {}
@@ -203,7 +211,8 @@ class LLMEngine:
                         for layer, ids in fb.record_routing.items():
                             c.req.routing.setdefault(layer, []).append(ids[o:o + n].cpu())
                     o += n
-        return self._commit(so, rows_req, tok, lp, mask)
+        with nvtx_range("commit"):
+            return self._commit(so, rows_req, tok, lp, mask)
 
     def _sync_bm_tokens(self, r: Request):
         n = self.bm.seq_len(r.seq_id)

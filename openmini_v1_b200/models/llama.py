@@ -226,10 +226,9 @@ class DecoderLM(nn.Module):
             ids = torch.cat([ids, ids.new_zeros(Tp - T)])
         h = self.embed_tokens(ids[sp.own_slice(Tp)]).contiguous()  # own residual rows
         k = 0
-        x = sp.reduce_norm(k, h, self.layers[0]["attn_norm"], cfg.rms_eps, Tp, has_partial=False)
+        x = sp.reduce_norm(k, h, self.layers[0]["attn_norm"], cfg.rms_eps, Tp, has_partial=False, wait=False)
         for i, L in enumerate(self.layers):
-            a = x[:T]
-            qkv = ops.linear(a, L["qkv"])
+            qkv = sp.linear_ag(x[:T], L["qkv"])
             ops.rope_kv(qkv, fb.positions, fb.slots, kv.k[i], kv.v[i], self.inv_freq, self.hq, self.hkv, self.hd,
                         cfg.rope_mode)
             if fb.prefill_tiles is not None and self.hd == 128:
@@ -240,12 +239,13 @@ class DecoderLM(nn.Module):
                                            self.hq, self.scale, fb.max_ctx)
             k += 1
             sp.linear_rs(attn.view(T, self.hq * self.hd), L["o"], k, Tp)
-            x = sp.reduce_norm(k, h, L["ffn_norm"], cfg.rms_eps, Tp, has_partial=True)
-            act = ops.silu_mul(ops.linear(x[:T], L["gate_up"]))
+            x = sp.reduce_norm(k, h, L["ffn_norm"], cfg.rms_eps, Tp, has_partial=True, wait=False)
+            act = ops.silu_mul(sp.linear_ag(x[:T], L["gate_up"]))
             k += 1
             sp.linear_rs(act, L["down"], k, Tp)
-            w_next = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
-            x = sp.reduce_norm(k, h, w_next, cfg.rms_eps, Tp, has_partial=True)
+            last = i + 1 == len(self.layers)
+            w_next = self.norm if last else self.layers[i + 1]["attn_norm"]
+            x = sp.reduce_norm(k, h, w_next, cfg.rms_eps, Tp, has_partial=True, wait=last)
         return x[:T].index_select(0, fb.logits_idx)
 
     def layer_forward(self, i, L, h, delta, fb: ForwardBatch, kv: KVCache):

@@ -137,14 +137,19 @@ class Q4Weight:
     def nbytes(self):
         return self.tiles.numel()
 
-    def linear(self, x, out=None, resid=None, peer=None):
+    def linear(self, x, out=None, resid=None, peer=None, agwait=None):
         if not x.is_cuda:
             y = ref.linear(x, self.dequantize().to(x.dtype), resid)
             if out is not None:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.tiles, None, 0, self.shape[0], out, resid, peer)
+        return _wq_linear(x, self.tiles, None, 0, self.shape[0], out, resid, peer, agwait)
+
+    def waits_in_kernel(self, M: int) -> bool:
+        """Whether a GEMM of M rows runs the decode kernel, which can wait for a
+        sequence-parallel gather itself (``agwait``)."""
+        return M <= 256 and (self.shape[1] // 64) % 4 == 0
 
 
 class Int8Weight:
@@ -189,7 +194,10 @@ class Int8Weight:
     def nbytes(self):
         return self.tiles.numel() + self.scale.numel() * 4
 
-    def linear(self, x, out=None, resid=None, peer=None):
+    def waits_in_kernel(self, M: int) -> bool:
+        return M <= 256 and (self.shape[1] // 64) % 2 == 0
+
+    def linear(self, x, out=None, resid=None, peer=None, agwait=None):
         if not x.is_cuda:
             y = (x.float() @ self.qweight.float().t()) * self.scale
             if resid is not None:
@@ -199,10 +207,10 @@ class Int8Weight:
                 out.copy_(y)
                 return out
             return y
-        return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid, peer)
+        return _wq_linear(x, self.tiles, self.scale, 1, self.shape[0], out, resid, peer, agwait)
 
 
-def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
+def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None, agwait=None):
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
@@ -215,6 +223,8 @@ def _wq_linear(x, tiles, scale, qtype, N, out, resid, peer=None):
     kw = {"sem": c.semaphores()}
     if peer is not None:
         kw["peer"] = peer
+    if agwait is not None:
+        kw["agwait"] = agwait
     _native.C().gemm_wq(x2, tiles, scale, qtype, out.view(-1, N), r2, ws, c.status, **kw)
     return out
 

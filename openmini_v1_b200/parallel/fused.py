@@ -30,9 +30,9 @@ def attach_tp_transport(model, par, device, kind: str = "symm", max_rows: int = 
     if par.tp <= 1:
         return None
     model.set_comm(make_tp_comm(par, device))
-    if kind == "symm":
+    if kind in ("symm", "symm_push"):
         from .symm import make_sp
-        model.set_sp(make_sp(par, device, max_rows=max_rows, dim=model.cfg.hidden_size))
+        model.set_sp(make_sp(par, device, max_rows=max_rows, dim=model.cfg.hidden_size, push=kind == "symm_push"))
     elif kind != "nccl":
         raise ValueError(f"unknown TP transport {kind!r}")
     return kind

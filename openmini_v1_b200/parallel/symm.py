@@ -69,7 +69,7 @@ class _SPBase:
 class SymmetricSP(_SPBase):
     """Peer-mapped buffers + fused reduce / RMSNorm / all-gather kernels (one process per GPU)."""
 
-    def __init__(self, group, device, max_rows: int, dim: int, push: bool = True):
+    def __init__(self, group, device, max_rows: int, dim: int, push: bool = False):
         self.push = push
         self.group = group
         self.world = dist.get_world_size(group)
@@ -121,17 +121,32 @@ class SymmetricSP(_SPBase):
         return ops.linear(x, w, out=out, peer=peer)
 
     def reduce_norm(self, k: int, h_own: torch.Tensor, w: torch.Tensor, eps: float, Tp: int,
-                    has_partial: bool) -> torch.Tensor:
+                    has_partial: bool, wait: bool = True) -> torch.Tensor:
+        """One event: sum the partials of the owned rows into the residual, RMSNorm, gather.
+        ``wait=False`` leaves the wait for the gathered rows to the consumer
+        (:meth:`linear_ag`)."""
         from .. import ops
         C = _native.C()
         status = ops.ctx(self.device).status
         pushed = has_partial and self.push
-        if not pushed:  # a peer-output GEMM published this event itself
-            C.sp_signal(self.bases, self.rank, status)
+        # pull mode: the reduce kernel opens the epoch and publishes this rank's partials
+        # itself; push mode: the peer-output GEMM did both
         C.sp_reduce_norm_gather(self.bases, self.rank, h_own, w, float(eps),
-                                self._off("p", k) if has_partial else -1, self._off("x", k), status, pushed)
-        C.sp_wait(self.bases, self.rank, status)
+                                self._off("p", k) if has_partial else -1, self._off("x", k), status, pushed,
+                                not pushed)
+        if wait:
+            C.sp_wait(self.bases, self.rank, status)
         return self.gathered(k, Tp)
+
+    def linear_ag(self, x: torch.Tensor, w):
+        """Column-parallel GEMM on rows gathered by ``reduce_norm(..., wait=False)``: a
+        weight-only decode GEMM waits for the gather inside the kernel (its weight stream
+        starts at once); any other GEMM runs after a separate wait kernel."""
+        from .. import ops
+        if getattr(w, "waits_in_kernel", None) is not None and w.waits_in_kernel(x.shape[0]):
+            return w.linear(x, agwait=[self.ptr, self.world])
+        _native.C().sp_wait(self.bases, self.rank, ops.ctx(self.device).status)
+        return ops.linear(x, w)
 
     def close(self):
         C = _native.C()
@@ -166,8 +181,12 @@ class EmulatedSP(_SPBase):
         from .. import ops
         return ops.linear(x, w, out=self.partial(k, Tp)[:x.shape[0]])
 
+    def linear_ag(self, x: torch.Tensor, w):
+        from .. import ops
+        return ops.linear(x, w)
+
     def reduce_norm(self, k: int, h_own: torch.Tensor, w: torch.Tensor, eps: float, Tp: int,
-                    has_partial: bool) -> torch.Tensor:
+                    has_partial: bool, wait: bool = True) -> torch.Tensor:
         own = self.own_slice(Tp)
         if has_partial:
             full = self._p[k & 1][:Tp].clone()
@@ -186,7 +205,7 @@ class EmulatedSP(_SPBase):
         pass
 
 
-def make_sp(par, device, max_rows: int, dim: int, dtype=torch.bfloat16, push: bool = True):
+def make_sp(par, device, max_rows: int, dim: int, dtype=torch.bfloat16, push: bool = False):
     """The sequence-parallel transport for this tensor-parallel group (None when tp == 1)."""
     if par.tp == 1:
         return None

@@ -78,12 +78,15 @@ def _worker(rank, world, port, q, wfmt, push):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("wfmt,push", [("bf16", True), ("bf16", False), ("q4", True)])
+@pytest.mark.parametrize("wfmt,push", [("bf16", True), ("bf16", False), ("q4", True), ("q4", False),
+                                       ("int8", False)])
 def test_sp_transport_matches_allreduce(wfmt, push):
     """push=True: the row-parallel GEMMs store their output tiles into the owner ranks'
     partials slots over NVLink and publish the epoch themselves (fused GEMM ->
-    reduce-scatter); push=False: local partials pulled by the reduce kernel."""
-    world = min(torch.cuda.device_count(), 4)
+    reduce-scatter); push=False (the default): local partials pulled by the reduce kernel,
+    which also publishes them, and weight-only GEMMs wait for the gathered rows inside
+    the kernel. Runs on every visible GPU (up to the transport's 8 ranks)."""
+    world = min(torch.cuda.device_count(), 8)
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
