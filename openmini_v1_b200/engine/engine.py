@@ -117,10 +117,10 @@ class LLMEngine:
         need = self.cfg.max_num_seqs * self.max_blocks_per_seq + 1
         if not self.is_cuda:
             return max(64, need)
-        per = self.model.kv_bytes_per_block()
+        from ..hardware.memory import kv_block_budget
         free, total = torch.cuda.mem_get_info(self.device)
-        budget = free - (1 - self.cfg.gpu_memory_utilization) * total - (4 << 30)
-        return int(max(64, min(need, budget // per)))
+        budget = kv_block_budget(free, total, self.model.kv_bytes_per_block(), self.cfg.gpu_memory_utilization)
+        return int(max(64, min(need, budget)))
 
     # ---------------------------------------------------------------- API
     def add_request(self, request_id: str, prompt_token_ids, params: SamplingParams | None = None,
