@@ -64,6 +64,10 @@ void om_sp_reduce_norm_gather(std::vector<int64_t> bases, int64_t rank, torch::T
                               double eps, int64_t p_off, int64_t x_off, torch::Tensor status, bool push,
                               bool signal);
 void om_sp_wait(std::vector<int64_t> bases, int64_t rank, torch::Tensor status);
+int64_t om_mla_workspace(int64_t rows, int64_t H, int64_t max_ctx);
+void om_mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor row_seq,
+                   torch::Tensor row_ctx, torch::Tensor out, torch::Tensor ws, int64_t max_ctx, double scale,
+                   torch::Tensor status);
 
 void om_moe_route(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> forced, torch::Tensor ids,
                   torch::Tensor wts, torch::Tensor counts);
@@ -128,4 +132,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bases"), py::arg("rank"), py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("p_off"),
         py::arg("x_off"), py::arg("status"), py::arg("push") = false, py::arg("signal") = false);
   m.def("sp_wait", &om_sp_wait, "wait until every rank pushed its normed rows for this epoch");
+  m.def("mla_workspace", &om_mla_workspace, "fp32 workspace floats of mla_decode");
+  m.def("mla_decode", &om_mla_decode, "latent attention over a paged 576-wide latent cache (absorbed form)");
 }

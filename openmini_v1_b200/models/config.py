@@ -43,6 +43,18 @@ class DSAConfig:
 
 
 @dataclass
+class MLAConfig:
+    """Multi-head latent attention: a 512-wide KV latent plus a 64-wide shared RoPE key
+    per token (the kernel's fixed widths), per-head no-RoPE query / key width and value
+    width; head_dim of the model is ignored for MLA layers."""
+    enabled: bool = False
+    kv_lora_rank: int = 512
+    qk_nope_dim: int = 128
+    qk_rope_dim: int = 64
+    v_head_dim: int = 128
+
+
+@dataclass
 class ModelConfig:
     name: str = "custom"
     vocab_size: int = 32000
@@ -60,6 +72,7 @@ class ModelConfig:
     dtype: str = "bfloat16"
     moe: MoEConfig = field(default_factory=MoEConfig)
     dsa: DSAConfig = field(default_factory=DSAConfig)
+    mla: MLAConfig = field(default_factory=MLAConfig)
     architecture: str = "llama"
     # sliding-window attention (Gemma-style local layers): 0 = off; with a window,
     # layer i is local unless (i + 1) % sliding_window_global_every == 0 (0: every layer local)
@@ -104,7 +117,8 @@ class ModelConfig:
         d = dict(d)
         moe = MoEConfig(**d.pop("moe", {}))
         dsa = DSAConfig(**d.pop("dsa", {}))
-        return ModelConfig(moe=moe, dsa=dsa, **d)
+        mla = MLAConfig(**d.pop("mla", {}))
+        return ModelConfig(moe=moe, dsa=dsa, mla=mla, **d)
 
 
 def tiny() -> ModelConfig:

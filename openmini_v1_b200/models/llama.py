@@ -85,6 +85,10 @@ class DecoderLM(nn.Module):
         self.vocab_local = cfg.vocab_size // tp if cfg.vocab_size % tp == 0 else cfg.vocab_size
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.inv_freq = ref.inv_freq(cfg.head_dim, cfg.rope_theta).to(self.device)
+        if cfg.mla.enabled:
+            if cfg.mla.kv_lora_rank != 512 or cfg.mla.qk_rope_dim != 64:
+                raise ValueError("MLA: the latent kernel takes kv_lora_rank 512 and qk_rope_dim 64")
+            self.mla_inv_freq = ref.inv_freq(cfg.mla.qk_rope_dim, cfg.rope_theta).to(self.device)
         self.weight_format = weight_format
         self.layers = []
         self._comm = None
@@ -120,9 +124,13 @@ class DecoderLM(nn.Module):
             L = {
                 "attn_norm": torch.ones(D, dtype=self.dtype, device=self.device),
                 "ffn_norm": torch.ones(D, dtype=self.dtype, device=self.device),
-                "qkv": self._randn(gen, (self.hq + 2 * self.hkv) * self.hd, D, std=std),
-                "o": self._randn(gen, D, self.hq * self.hd, std=std),
             }
+            if cfg.mla.enabled:
+                from .mla import init_mla
+                init_mla(self, L, gen, shared, std)
+            else:
+                L["qkv"] = self._randn(gen, (self.hq + 2 * self.hkv) * self.hd, D, std=std)
+                L["o"] = self._randn(gen, D, self.hq * self.hd, std=std)
             if cfg.moe.is_moe_layer(i):
                 E, Fe = cfg.moe.num_experts, cfg.moe.expert_ffn
                 L["router"] = self._randn(shared, E + cfg.moe.num_zero_experts, D, std=std)
@@ -147,12 +155,17 @@ class DecoderLM(nn.Module):
     # ------------------------------------------------------------------ cache
     def kv_bytes_per_block(self) -> int:
         el = torch.finfo(self.dtype).bits // 8
-        per = 2 * self.hkv * 16 * self.hd * el
+        per = (16 * 576 * el) if self.cfg.mla.enabled else 2 * self.hkv * 16 * self.hd * el
         if self.cfg.dsa.enabled:
             per += 16 * self.cfg.dsa.indexer_dim * el
         return per * self.cfg.num_layers
 
     def allocate_kv(self, num_blocks: int) -> KVCache:
+        if self.cfg.mla.enabled:  # one 576-wide latent row per token; no separate values
+            k = [torch.zeros(num_blocks, 16, 576, dtype=self.dtype, device=self.device)
+                 for _ in range(self.cfg.num_layers)]
+            v = [torch.zeros(num_blocks, 0, dtype=self.dtype, device=self.device) for _ in range(self.cfg.num_layers)]
+            return KVCache(k=k, v=v, num_blocks=num_blocks)
         shape = (num_blocks, self.hkv, 16, self.hd)
         k = [torch.zeros(shape, dtype=self.dtype, device=self.device) for _ in range(self.cfg.num_layers)]
         v = [torch.zeros(shape, dtype=self.dtype, device=self.device) for _ in range(self.cfg.num_layers)]
@@ -182,7 +195,7 @@ class DecoderLM(nn.Module):
         self._sp = sp
 
     def _use_sp(self, T: int) -> bool:
-        return (self._sp is not None and self._sp.fits(T) and not self.cfg.dsa.enabled
+        return (self._sp is not None and self._sp.fits(T) and not self.cfg.dsa.enabled and not self.cfg.mla.enabled
                 and self.cfg.sliding_window <= 0
                 and not any("router" in L for L in self.layers))
 
@@ -252,6 +265,10 @@ class DecoderLM(nn.Module):
         cfg = self.cfg
         T = h.shape[0]
         a = ops.rmsnorm(h, L["attn_norm"], cfg.rms_eps, delta=delta)
+        if cfg.mla.enabled:
+            from .mla import mla_attention
+            attn = mla_attention(self, i, L, a, fb, kv)
+            return self._after_attention(i, L, a, h, attn, fb)
         qkv = ops.linear(a, L["qkv"])
         ops.rope_kv(qkv, fb.positions, fb.slots, kv.k[i], kv.v[i], self.inv_freq, self.hq, self.hkv, self.hd,
                     cfg.rope_mode)
@@ -268,6 +285,10 @@ class DecoderLM(nn.Module):
             attn = ops.paged_attention(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx, self.hq,
                                        self.scale, fb.max_ctx)
         attn = attn.view(T, self.hq * self.hd)
+        return self._after_attention(i, L, a, h, attn, fb)
+
+    def _after_attention(self, i, L, a, h, attn, fb: ForwardBatch):
+        cfg = self.cfg
         if cfg.architecture == "openmini-quirk":
             h = a.clone()
         if self.par.tp == 1:

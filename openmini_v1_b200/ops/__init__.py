@@ -192,6 +192,25 @@ def kv_write(k, v, slots, k_cache, v_cache):
     _native.C().kv_write(k, v, slots, k_cache, v_cache)
 
 
+def mla_decode(q, cache, block_tables, row_seq, row_ctx, max_ctx, scale, out=None):
+    """Latent attention (absorbed MLA) of q [rows, H, 576] over the paged latent cache
+    [blocks, 16, 576] -> [rows, H, 512] (see ``csrc/attn/mla.cu``)."""
+    if not q.is_cuda:
+        o = ref.mla_decode(q, cache, block_tables, row_seq, row_ctx, scale)
+        if out is not None:
+            out.copy_(o)
+            return out
+        return o
+    rows, H = q.shape[0], q.shape[1]
+    if out is None:
+        out = torch.empty(rows, H, 512, dtype=q.dtype, device=q.device)
+    c = ctx(q.device)
+    ws = c.workspace("mla", _native.C().mla_workspace(rows, H, int(max_ctx)))
+    _native.C().mla_decode(q.contiguous(), cache, block_tables, row_seq, row_ctx, out, ws, int(max_ctx),
+                           float(scale), c.status)
+    return out
+
+
 def paged_attention(q, k_cache, v_cache, block_tables, row_seq, row_ctx, Hq, scale, max_ctx, out=None, impl=None):
     """Attention of query rows over the paged cache. ``max_ctx`` bounds the split count.
 

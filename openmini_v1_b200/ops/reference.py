@@ -267,3 +267,21 @@ def repetition_penalty(logits, prev, penalty):
             x = float(logits[b, tid])
             logits[b, tid] = x / pen if x > 0 else x * pen
     return logits
+
+
+def mla_decode(q, cache, block_tables, row_seq, row_ctx, scale):
+    """Absorbed-form latent attention. q [rows, H, 576] (512 latent | 64 rope), cache
+    [blocks, 16, 576]; row r attends to the first row_ctx[r] latent rows of its
+    sequence -> o_lat [rows, H, 512] = softmax(q . row * scale) @ row[:, :512]."""
+    rows, H, _ = q.shape
+    out = torch.zeros(rows, H, 512, dtype=q.dtype, device=q.device)
+    for r in range(rows):
+        n = int(row_ctx[r])
+        if n == 0:
+            continue
+        bt = block_tables[int(row_seq[r])]
+        idx = torch.arange(n, device=cache.device)
+        rows_kv = cache[bt[(idx // BLOCK).long()].long(), idx % BLOCK].float()  # [n, 576]
+        s = (q[r].float() @ rows_kv.t()) * scale
+        out[r] = (torch.softmax(s, -1) @ rows_kv[:, :512]).to(q.dtype)
+    return out

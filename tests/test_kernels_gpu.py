@@ -507,3 +507,51 @@ def test_paged_attention_context_bounds(impl):
         torch.cuda.synchronize()
         with pytest.raises(RuntimeError, match="status 5"):
             ops.check_status()
+
+
+@pytest.mark.parametrize("H,ctxs", [(16, [1, 64, 65, 300]), (128, [1000, 17]), (40, [129, 2048, 5])])
+def test_mla_decode_latent_attention(H, ctxs):
+    """Absorbed MLA attention over the paged 576-wide latent cache against the fp32
+    statement; a row whose context exceeds its block table reports OM_ERR_BOUNDS."""
+    rows = len(ctxs)
+    mb = (max(ctxs) + 15) // 16
+    nb = rows * mb + 3
+    cache = _rand(nb, 16, 576, seed=700)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(1)).to(DEV).int()
+    bt = perm[: rows * mb].view(rows, mb).contiguous()
+    q = _rand(rows, H, 576, seed=701, std=0.3)
+    row_seq = torch.arange(rows, dtype=torch.int32, device=DEV)
+    row_ctx = torch.tensor(ctxs, dtype=torch.int32, device=DEV)
+    scale = 1.0 / math.sqrt(192)
+    got = ops.mla_decode(q, cache, bt, row_seq, row_ctx, max(ctxs), scale)
+    torch.cuda.synchronize()
+    ops.check_status()
+    want = ref.mla_decode(q.float(), cache.float(), bt, row_seq, row_ctx, scale)
+    _close(got, want)
+    bad = torch.tensor([mb * 16 + 5] + ctxs[1:], dtype=torch.int32, device=DEV)
+    ops.mla_decode(q, cache, bt, row_seq, bad, mb * 16 + 5, scale)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError):
+        ops.check_status()
+
+
+def test_mla_layer_gpu_matches_fp32():
+    from openmini_v1_b200.models.config import MLAConfig, tiny
+    from openmini_v1_b200.models.llama import DecoderLM, ForwardBatch
+    from openmini_v1_b200.models.mla import mla_attention, mla_reference_layer
+    cfg = tiny()
+    cfg.dtype = "bfloat16"
+    cfg.mla = MLAConfig(enabled=True, qk_nope_dim=128, qk_rope_dim=64, v_head_dim=128)
+    m = DecoderLM(cfg, device=DEV, seed=1)
+    T = 70
+    i32 = dict(dtype=torch.int32, device=DEV)
+    fb = ForwardBatch(torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(T, **i32),
+                      torch.arange(5, **i32)[None], torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T,
+                      torch.tensor([T - 1], device=DEV))
+    kv = m.allocate_kv(5)
+    a = _rand(T, cfg.hidden_size, seed=702)
+    got = mla_attention(m, 0, m.layers[0], a, fb, kv)
+    torch.cuda.synchronize()
+    ops.check_status()
+    want = mla_reference_layer(m, m.layers[0], a, fb.positions)
+    _close(got, want, rtol=3e-2, atol=3e-2)
