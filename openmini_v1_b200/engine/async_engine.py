@@ -40,9 +40,9 @@ class AsyncLLMEngine:
                 while True:
                     kind, payload = self._inbox.get_nowait()
                     if kind == "add":
-                        rid, toks, params, sink, prio = payload
+                        rid, toks, params, sink, prio, img = payload
                         try:
-                            eng.add_request(rid, toks, params, priority=prio)
+                            eng.add_request(rid, toks, params, priority=prio, image_embeds=img)
                             self._subs[rid] = sink
                         except Exception as e:  # invalid request: report to its caller only
                             sink(("error", str(e)))
@@ -83,17 +83,17 @@ class AsyncLLMEngine:
 
     # ------------------------------------------------------------ client side
     def submit(self, prompt_token_ids, params: SamplingParams, sink, request_id: str | None = None,
-               priority: int = 0) -> str:
+               priority: int = 0, image_embeds: tuple | None = None) -> str:
         rid = request_id or f"req-{next(self._ids)}"
         params.validate()
-        self._inbox.put(("add", (rid, list(prompt_token_ids), params, sink, priority)))
+        self._inbox.put(("add", (rid, list(prompt_token_ids), params, sink, priority, image_embeds)))
         return rid
 
     def abort(self, request_id: str):
         self._inbox.put(("abort", request_id))
 
     async def generate(self, prompt_token_ids, params: SamplingParams, request_id: str | None = None,
-                       priority: int = 0):
+                       priority: int = 0, image_embeds: tuple | None = None):
         """Async iterator of RequestOutput (one per generated token)."""
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
@@ -101,7 +101,7 @@ class AsyncLLMEngine:
         def sink(item):
             loop.call_soon_threadsafe(q.put_nowait, item)
 
-        rid = self.submit(prompt_token_ids, params, sink, request_id, priority)
+        rid = self.submit(prompt_token_ids, params, sink, request_id, priority, image_embeds)
         try:
             while True:
                 kind, val = await q.get()

@@ -124,11 +124,20 @@ class LLMEngine:
 
     # ---------------------------------------------------------------- API
     def add_request(self, request_id: str, prompt_token_ids, params: SamplingParams | None = None,
-                    priority: int = 0) -> Request:
+                    priority: int = 0, image_embeds: tuple | None = None) -> Request:
+        """``image_embeds`` = (first prompt position, features [n, hidden]): the embeddings of
+        those n prompt positions are replaced by the features (vision input). The ids at
+        those positions should identify the image (see ``models.vision.splice_image``):
+        the prefix cache keys on ids."""
         params = params or SamplingParams()
         params.validate()
         req = Request(request_id=request_id, prompt_token_ids=[int(t) for t in prompt_token_ids],
                       params=params, priority=priority)
+        if image_embeds is not None:
+            p0, emb = image_embeds
+            if p0 < 0 or p0 + emb.shape[0] > len(req.prompt_token_ids):
+                raise ValueError("image features fall outside the prompt")
+            req.image_embeds = (int(p0), emb.to(self.device, self.model.dtype))
         self.sched.add(req)
         self.requests[request_id] = req
         return req
@@ -195,7 +204,8 @@ class LLMEngine:
         with nvtx_range("build"):
             fb, samp, rows_req = self._build(so)
         want_routing = any(c.req.params.return_routing for c in so.chunks)
-        if (so.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(so.chunks))
+        if (so.kind == "decode" and fb.embed_override is None and self.graphs is not None
+                and self.graphs.can_run(len(so.chunks))
                 and not self._needs_eager_sampling(rows_req) and not want_routing):
             with nvtx_range("decode_graph"):
                 tok, lp, mask = self.graphs.run(fb, samp, len(so.chunks))
@@ -344,6 +354,20 @@ class LLMEngine:
             max_ctx=(self.cfg.max_model_len if so.kind == "decode" else max(c.end for c in chunks)),
             logits_idx=d[5 * T + S * mb:o_t],
             prefill_tiles=d[o_t:n_i32].view(-1, 4) if tiles else None)
+        ov_rows, ov_emb = [], []
+        o = 0
+        for c in chunks:
+            ie = c.req.image_embeds
+            n = c.end - c.start
+            if ie is not None:
+                p0, emb = ie
+                a, b = max(c.start, p0), min(c.end, p0 + emb.shape[0])
+                if a < b:
+                    ov_rows.append(torch.arange(o + a - c.start, o + b - c.start))
+                    ov_emb.append(emb[a - p0:b - p0])
+            o += n
+        if ov_rows:
+            fb.embed_override = (torch.cat(ov_rows).to(self.device), torch.cat(ov_emb))
         # sampling knobs
         B = len(rows_req)
         f = st.f32.numpy()

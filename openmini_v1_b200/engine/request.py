@@ -71,6 +71,9 @@ class Request:
     finish_reason: str | None = None
     num_preemptions: int = 0
     rng_offset: int = 0
+    # multimodal prompt: (first prompt position, features [n, hidden]) replacing the
+    # embeddings of positions [first, first + n)
+    image_embeds: tuple | None = None
 
     @property
     def all_token_ids(self):

@@ -4,8 +4,10 @@ Behaviour of the reference's OpenMiniService
 (openmini-server/src/service/grpc/server.rs:43-383,1114): Chat builds a prompt
 from the session's stored memory plus the request messages ("role: content"
 lines) and streams one ChatResponse per generated token, finishing with usage;
-HealthCheck reports engine state. Image / speech RPCs need encoders that this
-server does not load: they answer UNIMPLEMENTED instead of synthetic output.
+HealthCheck reports engine state. ImageUnderstanding(-Stream) run the vision
+encoder and the engine when the server was started with one (``vision``);
+otherwise they, and the speech RPCs, answer UNIMPLEMENTED instead of synthetic
+output.
 Session memory is kept in SQLite (the reference's database), see ``SessionStore``.
 """
 from __future__ import annotations
@@ -52,7 +54,9 @@ class SessionStore:
 
 
 class OpenMiniServicer:
-    def __init__(self, aengine, tokenizer, store: SessionStore | None = None, metrics=None, default_max_tokens=256):
+    def __init__(self, aengine, tokenizer, store: SessionStore | None = None, metrics=None, default_max_tokens=256,
+                 vision=None):
+        self.vision = vision
         self.aengine = aengine
         self.tok = tokenizer
         self.store = store or SessionStore()
@@ -88,6 +92,24 @@ class OpenMiniServicer:
     async def HealthCheck(self, request, context):
         ok = self.aengine.alive and self.aengine.error is None
         return proto.HealthResponse(healthy=ok, message="ok" if ok else repr(self.aengine.error))
+
+    async def ImageUnderstanding(self, request, context):
+        if self.vision is None:
+            await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no vision encoder loaded")
+        try:
+            text, _, _ = await self.vision.answer(request.image_data, request.question)
+        except Exception as e:
+            await context.abort(grpc.StatusCode.INVALID_ARGUMENT, f"image: {e}")
+        return proto.ImageResponse(session_id=request.session_id, token=text, finished=True)
+
+    async def ImageUnderstandingStream(self, request, context):
+        if self.vision is None:
+            await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no vision encoder loaded")
+        try:
+            async for piece, fin, _, _ in self.vision.stream(request.image_data, request.question):
+                yield proto.ImageResponse(session_id=request.session_id, token=piece, finished=fin)
+        except Exception as e:
+            await context.abort(grpc.StatusCode.INVALID_ARGUMENT, f"image: {e}")
 
     async def _unimplemented(self, request, context):
         await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no vision / speech encoder loaded")

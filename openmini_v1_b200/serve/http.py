@@ -9,7 +9,8 @@ openmini-server/src/service/http/server.rs:213-268): ``chat``,
 ``chat/stream`` (SSE), ``health``, ``models``, ``metrics``,
 ``inference/{compute,batch,stats,config,reset}``. The reference answers chat
 with placeholder strings; here every chat route runs the engine. Image /
-speech routes need encoders that this server does not load and answer 501.
+speech routes need encoders that this server does not load and answer 501;
+/api/v1/image/understand runs the vision encoder when one is loaded.
 """
 from __future__ import annotations
 
@@ -43,7 +44,7 @@ def chat_prompt(messages) -> str:
 
 
 def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metrics | None = None,
-               config=None, trainer_factory=None) -> FastAPI:
+               config=None, trainer_factory=None, vision=None) -> FastAPI:
     app = FastAPI(title="openmini_v1_b200")
     metrics = metrics or Metrics()
     metrics.model_loaded.set(1)
@@ -252,7 +253,22 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
             e.stats[k] = 0
         return {"status": "ok"}
 
-    for path in ("/api/v1/image/understand", "/api/v1/tts", "/api/v1/stt"):
+    @app.post("/api/v1/image/understand")
+    async def image_understand(body: dict):
+        """{"image": base64 bytes, "question": str, "max_tokens"?: int, "temperature"?: float}"""
+        if vision is None:
+            return JSONResponse({"error": "/api/v1/image/understand needs a vision encoder, which is not loaded"},
+                                status_code=501)
+        import base64
+        try:
+            data = base64.b64decode(body["image"])
+            text, pt, n = await vision.answer(data, str(body.get("question", "Describe the image.")),
+                                              int(body.get("max_tokens", 0)), float(body.get("temperature", 0.0)))
+        except (KeyError, ValueError, OSError) as e:
+            return JSONResponse({"error": f"bad image request: {e}"}, status_code=400)
+        return {"answer": text, "usage": {"prompt_tokens": pt, "completion_tokens": n, "total_tokens": pt + n}}
+
+    for path in ("/api/v1/tts", "/api/v1/stt"):
         async def _ni(path=path):
             return JSONResponse({"error": f"{path} needs a vision / speech encoder, which is not loaded"},
                                 status_code=501)

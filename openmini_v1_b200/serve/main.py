@@ -69,12 +69,20 @@ async def serve(args):
     eng, tok = build_engine(cfg, args.preset, args.model)
     aeng = AsyncLLMEngine(eng)
     metrics = Metrics()
-    app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg)
+    vision = None
+    if args.vision:
+        from ..models.vision import VisionConfig, VisionEncoder
+        from .vision_service import ImageUnderstanding
+        vc = VisionConfig(lm_hidden=eng.model.cfg.hidden_size)
+        if eng.device.type == "cpu":
+            vc.hidden_size, vc.num_layers, vc.mlp_size, vc.num_heads = 256, 2, 512, 2
+        vision = ImageUnderstanding(aeng, tok, VisionEncoder(vc, device=eng.device, dtype=eng.model.dtype))
+    app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg, vision=vision)
     import uvicorn
     http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
                                          log_level="warning"))
     store = SessionStore(cfg.database.path if args.db else ":memory:")
-    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics),
+    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision),
                                                  f"{cfg.server.host}:{args.grpc_port or cfg.server.port}",
                                                  cfg.grpc.max_message_size_mb)
     gw = Gateway(aeng, tok, cfg.server.max_connections)
@@ -105,6 +113,8 @@ def main(argv=None):
     p.add_argument("--grpc-port", type=int, default=None)
     p.add_argument("--gateway-port", type=int, default=None)
     p.add_argument("--db", action="store_true", help="persist chat sessions to [database].path")
+    p.add_argument("--vision", action="store_true",
+                   help="load a vision encoder (random-init weights) and serve image understanding")
     args = p.parse_args(argv)
     init_logging()
     asyncio.run(serve(args))

@@ -1,0 +1,67 @@
+"""Image understanding for the serving API: decode the uploaded image, run the
+vision encoder, splice its features into the prompt and generate with the engine.
+
+The features replace ``num_patches`` placeholder positions of the prompt. The ids
+written at those positions are derived from the image bytes (a hash per position),
+so the engine's prefix cache, which keys on ids, reuses a cached prefix only for
+the same image and never across different images.
+
+Reference counterpart: the ImageUnderstanding / ImageUnderstandingStream RPCs and
+/api/v1/image/understand of openmini-server/src/service/grpc/server.rs:385-515 and
+service/http; the reference answers them with placeholder text.
+"""
+from __future__ import annotations
+
+import hashlib
+import io
+
+import numpy as np
+
+from ..engine.request import SamplingParams
+from ..engine.tokenizer import IncrementalDecoder
+
+
+def decode_image(data: bytes) -> np.ndarray:
+    """Encoded image bytes (PNG, JPEG, ... via Pillow) or a raw .npy [H, W, 3] array -> uint8 RGB."""
+    if data[:6] == b"\x93NUMPY":
+        return np.load(io.BytesIO(data))
+    from PIL import Image
+    return np.asarray(Image.open(io.BytesIO(data)).convert("RGB"))
+
+
+def image_ids(data: bytes, n: int, vocab: int, reserved: int = 256) -> list:
+    h = hashlib.blake2b(data, digest_size=16).digest()
+    base = int.from_bytes(h[:8], "little")
+    return [reserved + (base + i * 0x9E3779B97F4A7C15) % (vocab - reserved) for i in range(n)]
+
+
+class ImageUnderstanding:
+    def __init__(self, aengine, tokenizer, encoder, default_max_tokens: int = 256):
+        self.aengine, self.tok, self.enc = aengine, tokenizer, encoder
+        self.default_max = default_max_tokens
+        self.vocab = aengine.engine.model.cfg.vocab_size
+
+    def prepare(self, image_bytes: bytes, question: str):
+        """-> (prompt ids, (first image position, features [P, hidden]))."""
+        img = decode_image(image_bytes)
+        feats = self.enc(img)[0]
+        P = feats.shape[0]
+        head = self.tok.encode("user: <image>\n")
+        tail = self.tok.encode(f"{question}\nassistant:", add_bos=False)
+        ids = head + image_ids(image_bytes, P, self.vocab) + tail
+        return ids, (len(head), feats)
+
+    async def stream(self, image_bytes: bytes, question: str, max_tokens: int = 0, temperature: float = 0.0):
+        """Async iterator of (text piece, finished, prompt tokens, generated tokens)."""
+        ids, img = self.prepare(image_bytes, question)
+        sp = SamplingParams(temperature=max(temperature, 0.0), max_tokens=max_tokens or self.default_max)
+        dec, n = IncrementalDecoder(self.tok), 0
+        async for out in self.aengine.generate(ids, sp, image_embeds=img):
+            n += 1
+            yield dec.push(out.new_token_ids[0]), out.finished, len(ids), n
+
+    async def answer(self, image_bytes: bytes, question: str, max_tokens: int = 0, temperature: float = 0.0):
+        text, pt, n = [], 0, 0
+        async for piece, fin, pt, n in self.stream(image_bytes, question, max_tokens, temperature):
+            text.append(piece)
+        return "".join(text), pt, n

@@ -1,0 +1,98 @@
+"""Image understanding through the serving stack on CPU: image features spliced
+into the prompt through the engine match a full recompute with the same features,
+image-derived placeholder ids keep the prefix cache per image, and the HTTP and
+gRPC routes answer (501 / UNIMPLEMENTED without an encoder)."""
+import asyncio
+import base64
+import io
+
+import numpy as np
+import pytest
+import torch
+from fastapi.testclient import TestClient
+
+from openmini_v1_b200.engine.async_engine import AsyncLLMEngine
+from openmini_v1_b200.engine.engine import EngineConfig, LLMEngine
+from openmini_v1_b200.engine.request import SamplingParams
+from openmini_v1_b200.engine.tokenizer import ByteTokenizer
+from openmini_v1_b200.models.config import tiny
+from openmini_v1_b200.models.llama import DecoderLM, ForwardBatch
+from openmini_v1_b200.models.vision import VisionConfig, VisionEncoder
+from openmini_v1_b200.serve.http import create_app
+from openmini_v1_b200.serve.vision_service import ImageUnderstanding, image_ids
+
+
+def _npy(seed):
+    img = np.random.default_rng(seed).integers(0, 255, (40, 40, 3), dtype=np.uint8)
+    b = io.BytesIO()
+    np.save(b, img)
+    return b.getvalue()
+
+
+@pytest.fixture(scope="module")
+def vstack():
+    m = DecoderLM(tiny(), device="cpu", seed=0)
+    eng = LLMEngine(m, EngineConfig(max_num_seqs=4, max_model_len=256, enable_prefix_cache=True))
+    aeng = AsyncLLMEngine(eng)
+    tok = ByteTokenizer()
+    enc = VisionEncoder(VisionConfig(image_size=32, patch_size=16, hidden_size=128, num_layers=1, num_heads=2,
+                                     mlp_size=256, lm_hidden=256), device="cpu", dtype=torch.float32)
+    yield aeng, tok, m, ImageUnderstanding(aeng, tok, enc, default_max_tokens=4)
+    aeng.shutdown()
+
+
+def test_engine_image_rows_match_recompute(vstack):
+    aeng, tok, m, vis = vstack
+    ids, (p0, feats) = vis.prepare(_npy(1), "what is it?")
+    eng = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256, enable_prefix_cache=False))
+    r = eng.add_request("a", ids, SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True),
+                        image_embeds=(p0, feats))
+    while eng.has_unfinished():
+        eng.step()
+    toks = list(ids)
+    rows = torch.arange(p0, p0 + feats.shape[0])
+    for _ in range(3):
+        T = len(toks)
+        i32 = dict(dtype=torch.int32)
+        fb = ForwardBatch(torch.tensor(toks, **i32), torch.arange(T, **i32), torch.arange(T, **i32),
+                          torch.arange(16, **i32)[None], torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T,
+                          torch.tensor([T - 1]), embed_override=(rows, feats))
+        toks.append(int(m.logits(m(fb, m.allocate_kv(16))).argmax(-1)))
+    assert r.output_token_ids == toks[len(ids):]
+
+
+def test_image_ids_differ_per_image():
+    a, b = image_ids(_npy(1), 4, 32000), image_ids(_npy(2), 4, 32000)
+    assert a != b and a == image_ids(_npy(1), 4, 32000) and min(a + b) >= 256
+
+
+def test_http_and_grpc_image_routes(vstack):
+    aeng, tok, m, vis = vstack
+    c = TestClient(create_app(aeng, tok, "tiny", vision=vis))
+    r = c.post("/api/v1/image/understand", json={"image": base64.b64encode(_npy(3)).decode(), "question": "?",
+                                                 "max_tokens": 3})
+    assert r.status_code == 200, r.text
+    assert r.json()["usage"]["completion_tokens"] == 3
+    assert c.post("/api/v1/image/understand", json={"image": "AAAA"}).status_code == 400
+    assert TestClient(create_app(aeng, tok, "tiny")).post("/api/v1/image/understand",
+                                                          json={"image": ""}).status_code == 501
+    import grpc
+    from openmini_v1_b200.serve import proto
+    from openmini_v1_b200.serve.grpc_server import OpenMiniServicer, start_grpc_server
+
+    async def run():
+        server, port = await start_grpc_server(OpenMiniServicer(aeng, tok, vision=vis), "127.0.0.1:0")
+        try:
+            async with grpc.aio.insecure_channel(f"127.0.0.1:{port}") as ch:
+                req = proto.ImageRequest(session_id="s", image_data=_npy(4), question="?")
+                ser = proto.message("ImageRequest").SerializeToString
+                de = proto.message("ImageResponse").FromString
+                one = await ch.unary_unary(f"/{proto.SERVICE}/ImageUnderstanding", request_serializer=ser,
+                                           response_deserializer=de)(req)
+                assert one.finished and one.session_id == "s"
+                outs = [o async for o in ch.unary_stream(f"/{proto.SERVICE}/ImageUnderstandingStream",
+                                                         request_serializer=ser, response_deserializer=de)(req)]
+                assert len(outs) == 4 and outs[-1].finished and "".join(o.token for o in outs) == one.token
+        finally:
+            await server.stop(1)
+    asyncio.run(run())
