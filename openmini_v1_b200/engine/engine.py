@@ -49,6 +49,7 @@ class EngineConfig:
     seed: int = 0
     speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
     draft_engine: object = None            # with speculative_k: an LLMEngine of a draft model proposes instead
+    mtp_head: object = None                # with speculative_k: a models.mtp.MTPHead proposes the drafts
     preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)
 
 
@@ -106,8 +107,12 @@ class LLMEngine:
         self.spec = None
         if self.cfg.speculative_k > 0:
             from .speculative import DraftModelProposer, NgramProposer
-            self.spec = (DraftModelProposer(self.cfg.draft_engine, self.cfg.speculative_k)
-                         if self.cfg.draft_engine is not None else NgramProposer(self.cfg.speculative_k))
+            if self.cfg.mtp_head is not None:
+                from ..models.mtp import MTPProposer
+                self.spec = MTPProposer(self.cfg.mtp_head, self.cfg.speculative_k)
+            else:
+                self.spec = (DraftModelProposer(self.cfg.draft_engine, self.cfg.speculative_k)
+                             if self.cfg.draft_engine is not None else NgramProposer(self.cfg.speculative_k))
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "preemptions": 0}
         if self.is_cuda and self.cfg.use_cuda_graph:
             from .cuda_graph import DecodeGraphs

@@ -10,6 +10,10 @@ plus the model's next token, so a step emits 1 .. m+1 tokens and the output
 is identical to plain greedy decoding. KV of rejected drafts sits in slots
 beyond the sequence length and is overwritten later.
 
+Proposers: n-gram lookup, a draft model (``DraftModelProposer``) or a
+multi-token-prediction head (``models.mtp.MTPProposer``, fed the hidden row
+behind each sequence's last emitted token after every verified step).
+
 Reference: draft / verify speculative decoding with adaptive k
 (openmini-server/src/model/inference/speculative.rs,
 speculative_decoding_v2.rs); the proposer here needs no draft model.
@@ -71,7 +75,7 @@ def eligible(r) -> bool:
             and not p.return_routing)
 
 
-def spec_decode_step(eng, so, proposer: NgramProposer) -> list:
+def spec_decode_step(eng, so, proposer) -> list:
     """One verified speculative step for a pure decode batch of greedy requests."""
     chunks = so.chunks
     rows_ids, rows_pos, rows_slot, rows_seq, rows_ctx = [], [], [], [], []
@@ -81,7 +85,10 @@ def spec_decode_step(eng, so, proposer: NgramProposer) -> list:
         p = r.num_tokens - 1
         room = min(proposer.k, r.params.max_tokens - len(r.output_token_ids) - 1,
                    eng.cfg.max_model_len - r.num_tokens - 1)
-        d = proposer.propose(r.all_token_ids, max(room, 0))
+        if getattr(proposer, "wants_request", False):
+            d = proposer.propose(r.all_token_ids, max(room, 0), req=r)
+        else:
+            d = proposer.propose(r.all_token_ids, max(room, 0))
         if d:
             try:
                 eng.bm.reserve(r.seq_id, len(d) + 1)
@@ -106,7 +113,9 @@ def spec_decode_step(eng, so, proposer: NgramProposer) -> list:
                       row_ctx=d[4 * T:5 * T], block_tables=torch.from_numpy(bt).to(dev),
                       max_ctx=eng.cfg.max_model_len, logits_idx=torch.arange(T, device=dev))
     eng.stage.h2d_bytes = host.numel() * 4 + bt.size * 4
-    greedy = eng.model.logits(eng.model(fb, eng.kv)).argmax(-1).to(torch.int32).cpu().tolist()
+    x = eng.model(fb, eng.kv)
+    greedy = eng.model.logits(x).argmax(-1).to(torch.int32).cpu().tolist()
+    observe = getattr(proposer, "observe", None)
     eng.stage.d2h_bytes = T * 4
     now = time.monotonic()
     outs = []
@@ -116,11 +125,12 @@ def spec_decode_step(eng, so, proposer: NgramProposer) -> list:
     for c, dr in zip(chunks, drafts):
         r = c.req
         g = greedy[o:o + len(dr) + 1]
-        o += len(dr) + 1
         a = 0
         while a < len(dr) and dr[a] == g[a]:
             a += 1
         new = dr[:a] + [g[a]]
+        last_row = o + a  # hidden row whose prediction is the last emitted token
+        o += len(dr) + 1
         eng.stats["spec_proposed"] += len(dr)
         eng.stats["spec_accepted"] += a
         r.num_computed = r.num_tokens
@@ -135,10 +145,14 @@ def spec_decode_step(eng, so, proposer: NgramProposer) -> list:
             reason = eng._stop_reason(r, int(t))
             if reason:
                 break
+        if observe is not None and not reason:
+            observe(r, x[last_row], g[a])
         if reason:
             r.finish_reason, r.finish_time = reason, now
             eng.sched.finish(r)
             eng.requests.pop(r.request_id, None)
+            if hasattr(proposer, "forget"):
+                proposer.forget(r)
         outs.append(RequestOutput(request_id=r.request_id, new_token_ids=emitted,
                                   output_token_ids=r.output_token_ids, finished=reason is not None,
                                   finish_reason=reason, prompt_tokens=len(r.prompt_token_ids)))
