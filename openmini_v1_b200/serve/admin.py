@@ -308,6 +308,13 @@ class AdminService:
     def mount(self, app: FastAPI):
         app.include_router(self.router())
 
+        @app.get("/admin/ui")
+        async def admin_ui():
+            """Static single-page admin console over the /admin REST API (no build step)."""
+            from fastapi.responses import HTMLResponse
+            import pathlib
+            return HTMLResponse((pathlib.Path(__file__).parent / "static" / "admin.html").read_text())
+
         @app.middleware("http")
         async def _sla(request: Request, call_next):
             t0 = time.perf_counter()

@@ -66,3 +66,22 @@ def test_sla_monitor():
         s.record(500.0, ok=False)
     r = s.report()
     assert not r["compliant"] and r["p99_ms"] == 500.0
+
+
+def test_admin_web_console_served_and_wired():
+    """The console page is served and every view it opens is a route of the admin API."""
+    import re
+    svc = AdminService(secret=b"k" * 32)
+    app = FastAPI()
+    svc.mount(app)
+    c = TestClient(app)
+    r = c.get("/admin/ui")
+    assert r.status_code == 200 and r.headers["content-type"].startswith("text/html")
+    html = r.text
+    assert "/admin/auth/login" in html and "Bearer" in html
+    routes = {getattr(rt, "path", "") for rt in app.routes}
+    for view in re.findall(r'data-view="([a-z]+)"', html):
+        assert f"/admin/{view}" in routes, view
+    tok = c.post("/admin/auth/login", json={"username": "admin", "password": "admin"}).json()["token"]
+    for view in re.findall(r'data-view="([a-z]+)"', html):
+        assert c.get(f"/admin/{view}", headers={"Authorization": f"Bearer {tok}"}).status_code == 200, view
