@@ -96,3 +96,30 @@ def test_fp8_kv_roundtrip():
     back = av.fp8_kv_dequantize(codes, s).float()
     rel = (back - c.float()).abs().max() / c.float().abs().max()
     assert rel < 0.07
+
+
+def test_blockffn_sparse_equals_dense_statement():
+    from openmini_v1_b200.models.moe_variants import BlockFFN
+    f = BlockFFN(hidden=64, ffn=256, chunks=8, threshold=0.8, seed=1)
+    x = torch.randn(30, 64, generator=torch.Generator().manual_seed(5))
+    y = f(x)
+    assert torch.allclose(y, f.dense_reference(x), atol=1e-5)
+    assert 0.0 < f.last_density < 1.0  # some chunks skipped, some run
+    f.thr = -1.0
+    assert f(x).shape == (30, 64) and f.last_density == 1.0
+
+
+def test_longcat_dual_branch():
+    from openmini_v1_b200.models.moe_variants import LongCatDualBranch
+    m = LongCatDualBranch(64, 128, 64, pivot=1000, width=100, skip_below=500, seed=2)
+    x = torch.randn(10, 64, generator=torch.Generator().manual_seed(6))
+    a, b = m.weights(100)
+    assert b < 1e-3 and abs(a + b - 1) < 1e-9
+    y_short = m(x, 100)
+    assert m.aux_evaluated == 0
+    y_long = m(x, 3000)
+    assert m.aux_evaluated == 1 and not torch.allclose(y_short, y_long)
+    a2, b2 = m.weights(3000)
+    from openmini_v1_b200.models.moe_variants import _swiglu
+    want = _swiglu(x, *m.main) * a2 + _swiglu(x, *m.aux) * b2
+    assert torch.allclose(y_long, want, atol=1e-6)
