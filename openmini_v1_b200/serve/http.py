@@ -205,24 +205,32 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
                 yield {"session_id": sid, "token": dec.push(out.new_token_ids[0]), "finished": out.finished}
         return sse(gen)
 
+    from ..models.hp_pipeline import HighPerformancePipeline
+    pipeline = HighPerformancePipeline()
+
     @app.post("/api/v1/inference/compute")
     async def api_compute(req: Request):
-        """Raw attention over client-supplied q, k, v ([seq, dim] lists), as the reference's
-        HighPerformancePipeline route; runs the fp32 statement on the host."""
+        """Raw attention over client-supplied q, k, v ([seq, dim] lists, or [seq, heads, head_dim])
+        through the high-performance pipeline on the engine's device (strategy chosen by length)."""
         import torch
         body = await req.json()
         try:
             q, k, v = (torch.tensor(body[n], dtype=torch.float32) for n in ("q", "k", "v"))
         except Exception:
-            raise HTTPException(400, "q, k, v must be 2-D numeric arrays")
-        if q.dim() != 2 or k.shape != v.shape or q.shape[1] != k.shape[1]:
+            raise HTTPException(400, "q, k, v must be numeric arrays")
+        if q.dim() == 2:
+            q, k, v = q[:, None], k[:, None], v[:, None]
+        if q.dim() != 3 or k.shape != v.shape or q.shape[2] != k.shape[2] or q.shape[1] % k.shape[1]:
             raise HTTPException(400, "shape mismatch")
+        dev = getattr(getattr(aengine, "engine", None), "device", torch.device("cpu"))
+        causal = bool(body.get("causal", False)) and q.shape[0] <= k.shape[0]
         t0 = time.time()
-        s = q @ k.t() / math.sqrt(q.shape[1])
-        if body.get("causal", False) and q.shape[0] == k.shape[0]:
-            s = s.masked_fill(torch.ones_like(s, dtype=torch.bool).triu(1), float("-inf"))
-        o = torch.softmax(s, -1) @ v
-        return {"output": o.tolist(), "strategy": "dense", "inference_time_ms": (time.time() - t0) * 1e3}
+        o, strat = pipeline.forward(q.to(dev), k.to(dev), v.to(dev), causal=causal)
+        o = o.cpu()
+        if o.shape[1] == 1 and len(body["q"]) and not isinstance(body["q"][0][0], list):
+            o = o[:, 0]
+        return {"output": o.tolist(), "strategy": strat, "inference_time_ms": (time.time() - t0) * 1e3,
+                "stats": {"calls": pipeline.stats.calls, "by_strategy": dict(pipeline.stats.by_strategy)}}
 
     @app.post("/api/v1/inference/batch")
     async def api_batch(req: Request):

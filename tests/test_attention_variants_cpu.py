@@ -123,3 +123,19 @@ def test_longcat_dual_branch():
     from openmini_v1_b200.models.moe_variants import _swiglu
     want = _swiglu(x, *m.main) * a2 + _swiglu(x, *m.aux) * b2
     assert torch.allclose(y_long, want, atol=1e-6)
+
+
+def test_hp_pipeline_strategies():
+    from openmini_v1_b200.models.hp_pipeline import HighPerfPipelineConfig, HighPerformancePipeline
+    p = HighPerformancePipeline(HighPerfPipelineConfig(streaming_threshold=64, window=16, sinks=2))
+    q, k, v = _qkv(T=40)
+    o, s = p.forward(q, k, v)
+    assert s == "flash" and torch.allclose(o, av.full_attention(q, k, v), atol=1e-5)
+    q, k, v = _qkv(T=100)
+    o, s = p.forward(q, k, v)
+    assert s == "streaming"
+    t = 80  # row 80 sees keys 0, 1 and 65..80
+    keep = [0, 1] + list(range(65, 81))
+    want = av.full_attention(q[t:t + 1], k[keep], v[keep], causal=False)
+    assert torch.allclose(o[t], want[0], atol=1e-5)
+    assert p.stats.by_strategy == {"flash": 1, "streaming": 1} and p.stats.calls == 2
