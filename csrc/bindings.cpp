@@ -31,7 +31,7 @@ void om_paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
 int64_t om_paged_attention_workspace(int64_t rows, int64_t Hq, int64_t D, int64_t max_ctx);
 void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
                torch::Tensor rng, torch::Tensor out_tok, c10::optional<torch::Tensor> out_logprob,
-               c10::optional<torch::Tensor> keep_mask, int64_t row0);
+               c10::optional<torch::Tensor> keep_mask);
 void om_repetition_penalty(torch::Tensor logits, torch::Tensor prev, torch::Tensor penalty);
 void om_decode_advance(torch::Tensor sampled, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx,
                        torch::Tensor slots, torch::Tensor bt, torch::Tensor rng, c10::optional<torch::Tensor> hist,
@@ -105,7 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_workspace", &om_paged_attention_workspace);
   m.def("sample", &om_sample, py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("top_k"),
         py::arg("rng"), py::arg("out_tok"), py::arg("out_logprob") = py::none(),
-        py::arg("keep_mask") = py::none(), py::arg("row0") = 0);
+        py::arg("keep_mask") = py::none());
   m.def("repetition_penalty", &om_repetition_penalty);
   m.def("decode_advance", &om_decode_advance);
   m.def("quantize_q4", &om_quantize_q4, py::arg("w"), py::arg("q"), py::arg("scales"),

@@ -60,8 +60,6 @@ struct SampleArgs {
   int* out_tok;
   float* out_logprob;
   uint32_t* keep_mask;  // [B, ceil(V/32)] or null
-  int row0;             // global index of row 0 (row-parallel sampling under TP): the draw of
-                        // row b uses counter row0 + b, so it does not depend on the split
 };
 
 // ---------------------------------------------------------------- cluster helpers
@@ -227,7 +225,9 @@ __global__ void __cluster_dims__(SCL, 1, 1) __launch_bounds__(SNT) sample_kernel
     if (keep) {
       float score = x[e] - mx;
       if (!greedy) {
-        uint32_t c[4] = {(uint32_t)i, (uint32_t)(a.row0 + b), (uint32_t)off, (uint32_t)(off >> 32)};
+        // counter (token, 0, offset) under key = the request's seed: a draw depends on the
+        // request's seed and step only, not on its row in the batch or the TP split
+        uint32_t c[4] = {(uint32_t)i, 0u, (uint32_t)off, (uint32_t)(off >> 32)};
         philox4x32_10(c, seed_lo, seed_hi);
         const float u = ((float)c[0] + 0.5f) * 2.3283064365386963e-10f;
         score -= logf(-logf(u));
@@ -309,7 +309,7 @@ static void launch_sample(const SampleArgs& a, int B, cudaStream_t st) {
 
 void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
                torch::Tensor rng, torch::Tensor out_tok, c10::optional<torch::Tensor> out_logprob,
-               c10::optional<torch::Tensor> keep_mask, int64_t row0) {
+               c10::optional<torch::Tensor> keep_mask) {
   TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [B, V]");
   const int B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
@@ -329,7 +329,6 @@ void om_sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor to
   a.out_tok = out_tok.data_ptr<int>();
   a.out_logprob = out_logprob.has_value() ? out_logprob->data_ptr<float>() : nullptr;
   a.keep_mask = nullptr;
-  a.row0 = (int)row0;
   if (keep_mask.has_value()) {
     TORCH_CHECK(keep_mask->numel() >= (int64_t)B * ((V + 31) / 32), "sample: keep_mask too small");
     a.keep_mask = reinterpret_cast<uint32_t*>(keep_mask->data_ptr<int>());

@@ -317,8 +317,8 @@ class DecoderLM(nn.Module):
         Under tensor parallelism with a vocabulary-sharded LM head the rows are sampled
         row-parallel instead of gathering every rank's logits everywhere: one all-to-all
         gives rank r the full-vocabulary logits of rows [r B'/W, (r+1) B'/W) (B' = B
-        padded to a multiple of W), each rank samples only those rows (global row index
-        in the random counter, so draws match an unsplit run), and one all-gather of
+        padded to a multiple of W), each rank samples only those rows (a draw depends on
+        the request's seed and step only, so it matches an unsplit run), and one all-gather of
         (token, logprob) pairs returns the result to every rank. Per rank this moves
         1/W of the logits and does 1/W of the sampling work."""
         W = self.par.tp
@@ -336,7 +336,7 @@ class DecoderLM(nn.Module):
         full = recv.permute(1, 0, 2).reshape(per, -1)
         r = self.par.tp_rank
         rows = slice(r * per, (r + 1) * per)
-        tok, lp, _ = ops.sample(full, *(k[rows] for k in knobs), want_mask=False, row0=r * per)
+        tok, lp, _ = ops.sample(full, *(k[rows] for k in knobs), want_mask=False)
         pair = torch.stack([tok, lp.view(torch.int32)], dim=1)  # [per, 2] int32
         allp = self._comm.all_gather(pair, dim=0)  # [Bp, 2]
         return allp[:B, 0].contiguous(), allp[:B, 1].contiguous().view(torch.float32), None

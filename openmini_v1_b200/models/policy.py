@@ -2,7 +2,9 @@
 
 Holds fp32 master parameters (``nn.Parameter``) of a decoder with the same
 architecture and weight layout as :class:`DecoderLM`, computes in bf16 on the
-GPU through the differentiable tcgen05 GEMM (``ops.autograd.linear``), and can
+GPU through the differentiable tcgen05 GEMM (``ops.autograd.linear``) and the
+differentiable FlashAttention (``ops.autograd.attention``: tcgen05 kernel forward,
+gradient recomputed from its log-sum-exp), and can
 push its weights into an inference ``DecoderLM`` (rollout weight sync).
 
 The forward takes whole sequences (no paged cache) and supports Keep-Routing
@@ -81,9 +83,7 @@ class Policy(nn.Module):
             v = qkv[..., (H + Hkv) * hd:].view(B, T, Hkv, hd)
             q = _rope(q, pos, self.inv_freq, cfg.rope_mode)
             k = _rope(k, pos, self.inv_freq, cfg.rope_mode)
-            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                               is_causal=True, enable_gqa=Hkv != H)
-            o = o.transpose(1, 2).reshape(B, T, H * hd)
+            o = ag.attention(q, k, v, 1.0 / math.sqrt(hd)).reshape(B, T, H * hd)
             x = x + ag.linear(o, self._w(L.o))
             h = ag.rmsnorm(x, self._w(L.ffn_norm), cfg.rms_eps)
             if L.is_moe:

@@ -257,19 +257,19 @@ def flash_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, tiles, Hq
     return out
 
 
-def sample(logits, temperature, top_p, top_k, rng, want_mask=False, row0: int = 0):
+def sample(logits, temperature, top_p, top_k, rng, want_mask=False):
     """Returns (tokens int32, logprob fp32, packed keep mask int32 [B, ceil(V/32)] or None).
 
-    ``row0``: global index of the first row (row-parallel sampling keeps every row's
-    random draw independent of how the rows are split across ranks)."""
+    Each row's random draw depends only on its request's (seed, offset): the same
+    request samples the same token whatever the batch or the tensor-parallel split."""
     B, V = logits.shape
     if not logits.is_cuda:
-        t, lp, m = ref.sample(logits, temperature, top_p, top_k, rng, row0=row0)
+        t, lp, m = ref.sample(logits, temperature, top_p, top_k, rng)
         return t, lp, (ref.pack_mask(m) if want_mask else None)
     tok = torch.empty(B, dtype=torch.int32, device=logits.device)
     lp = torch.empty(B, dtype=torch.float32, device=logits.device)
     mask = torch.empty(B, (V + 31) // 32, dtype=torch.int32, device=logits.device) if want_mask else None
-    _native.C().sample(logits, temperature, top_p, top_k, rng, tok, lp, mask, int(row0))
+    _native.C().sample(logits, temperature, top_p, top_k, rng, tok, lp, mask)
     return tok, lp, mask
 
 

@@ -204,10 +204,11 @@ def _cutoff_mask(x, k, p):
     return keep
 
 
-def sample(logits, temperature, top_p, top_k, rng, row0: int = 0):
+def sample(logits, temperature, top_p, top_k, rng):
     """Returns (tokens int32 [B], logprob fp32 [B], keep mask bool [B, V]).
 
-    Row b draws with Philox counter (token, row0 + b, offset) under key = seed."""
+    Row b draws with Philox counter (token, 0, offset) under key = its seed: the draw
+    depends on the request's (seed, offset) only, not on its position in the batch."""
     B, V = logits.shape
     toks = torch.empty(B, dtype=torch.int32)
     lps = torch.empty(B, dtype=torch.float32)
@@ -226,7 +227,7 @@ def sample(logits, temperature, top_p, top_k, rng, row0: int = 0):
             keep = _cutoff_mask(x, int(top_k[b]), float(top_p[b]))
             seed, off = int(rng[b][0]) & 0xFFFFFFFFFFFFFFFF, int(rng[b][1]) & 0xFFFFFFFFFFFFFFFF
             ids = np.arange(V, dtype=np.uint64)
-            c = philox4x32_10(ids, np.full(V, row0 + b), np.full(V, off & 0xFFFFFFFF), np.full(V, off >> 32),
+            c = philox4x32_10(ids, np.zeros(V, dtype=np.uint64), np.full(V, off & 0xFFFFFFFF), np.full(V, off >> 32),
                               seed & 0xFFFFFFFF, seed >> 32)
             u = (c[0].astype(np.float64) + 0.5) * 2.0 ** -32
             u = torch.from_numpy(u.astype(np.float32))

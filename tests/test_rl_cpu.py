@@ -78,3 +78,72 @@ def test_rollout_replay_and_update():
     stats = [tr.train_step(prompts) for _ in range(6)]
     assert all(st["tokens"] > 0 for st in stats)
     assert stats[-1]["reward_mean"] > stats[0]["reward_mean"], [st["reward_mean"] for st in stats]
+
+
+def _trainer(seed_offset=0, dp_group=None, train_batch=16):
+    cfg = small_moe()
+    pol = Policy(cfg, seed=1)
+    inf = DecoderLM(cfg, device="cpu", materialize=False)
+    inf.layers = [{} for _ in range(cfg.num_layers)]
+    eng = LLMEngine(inf, EngineConfig(max_num_seqs=16, max_model_len=128, enable_prefix_cache=False))
+    reward = SubsetFractionReward(cfg.vocab_size, size=60, seed=3)
+    return GRPOTrainer(pol, eng, reward, GRPOConfig(learning_rate=3e-3, group_size=4, kl_coef=0.04),
+                       max_new_tokens=8, temperature=1.0, top_p=0.9, dp_group=dp_group, train_batch=train_batch,
+                       seed_offset=seed_offset)
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, 300, (10,), generator=g).tolist() for _ in range(2)]
+
+
+def test_batched_logp_equals_per_sample():
+    tr = _trainer()
+    samples = tr.rollout(_prompts())
+    tr.train_batch = 1
+    one = tr._batch_logp(tr.policy, samples)
+    tr.train_batch = 8
+    many = tr._batch_logp(tr.policy, samples)
+    for a, b in zip(one, many):
+        assert torch.allclose(a, b, atol=1e-5)
+
+
+def _dp_worker(rank, port, q):
+    import os
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    tr = _trainer(seed_offset=rank, dp_group=dist.group.WORLD)
+    tr.train_step([_prompts()[rank]])
+    q.put((rank, {n: p.grad.numpy().copy() for n, p in tr.policy.named_parameters() if p.grad is not None}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_data_parallel_step_matches_single_process():
+    """Two gloo ranks with one prompt each (overlapped bucket all-reduce) end the step
+    with the gradients of one process that trains on both prompts (the reduced, clipped
+    gradients the optimizer used; Adam's first step is about lr * sign(g), which would
+    turn summation-order noise of near-zero entries into lr-sized parameter differences)."""
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_dp_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(60)
+    single = _trainer()
+    single.train_step(_prompts())
+    want = {n: p.grad for n, p in single.policy.named_parameters() if p.grad is not None}
+    for r in (0, 1):
+        assert res[r].keys() == want.keys()
+        for n, t in res[r].items():
+            scale = float(want[n].abs().max()) + 1e-12
+            assert torch.allclose(torch.from_numpy(t), want[n], atol=1e-4 * scale), (r, n)
