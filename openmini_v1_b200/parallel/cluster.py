@@ -301,6 +301,17 @@ PRESETS = {  # name -> (ModelSpec, default tp, pp)
 }
 
 
+def make_plan(spec: ModelSpec, tp: int, pp: int, gpus: int, gpu_mem_gb: float = 180.0,
+              kv_tokens: int = 256 * 4608, mem_util: float = 0.9, kv_bytes: int = 2) -> Plan:
+    """The memory footprint of one given (tp, pp) layout on ``gpus`` GPUs."""
+    kv_per_token = 2 * spec.layers * spec.kv_heads * spec.head_dim * kv_bytes
+    w = spec.params_b * spec.bytes_per_param / (tp * pp)
+    kv = kv_tokens * kv_per_token / 1e9 / (tp * pp)
+    ok = w + kv <= gpu_mem_gb * mem_util
+    return Plan(tp, pp, max(1, gpus // (tp * pp)), w, kv, ok,
+                f"tp{tp} pp{pp} dp{max(1, gpus // (tp * pp))}" + ("" if ok else ": does not fit"))
+
+
 def plan_parallelism(spec: ModelSpec, gpus: int, gpu_mem_gb: float = 180.0, nvlink_domain: int = 8,
                      kv_tokens: int = 256 * 4608, mem_util: float = 0.9, kv_bytes: int = 2) -> Plan:
     """Smallest TP (a power of two within one NVLink domain, dividing the KV heads when
