@@ -44,6 +44,8 @@ void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
 void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor icache, torch::Tensor bt,
                    torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor scores, torch::Tensor status);
 void om_dsa_topk(torch::Tensor scores, torch::Tensor row_ctx, int64_t k, torch::Tensor out_idx, torch::Tensor out_n);
+void om_dsa_head_reduce(torch::Tensor g, int64_t S, torch::Tensor w, int64_t H, torch::Tensor row_ctx,
+                        torch::Tensor scores);
 void om_flash_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor row_ctx, torch::Tensor tiles, torch::Tensor out, int64_t Hq, double scale,
                       torch::Tensor status, c10::optional<torch::Tensor> lse);
@@ -115,6 +117,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequant_int8", &om_dequant_int8);
   m.def("dsa_scores", &om_dsa_scores, "DSA indexer scores over the paged indexer-key cache");
   m.def("dsa_topk", &om_dsa_topk, "per-row top-k key positions");
+  m.def("dsa_head_reduce", &om_dsa_head_reduce, "indexer scores from the tensor-core head GEMM: relu, weights, mask");
   m.def("dsa_attention", &om_dsa_attention, "attention over selected keys of the paged cache");
   m.def("moe_route", &om_moe_route, "router top-k + softmax weights + per-expert counts");
   m.def("moe_permute", &om_moe_permute, "expert offsets and expert-sorted copy of the activations");

@@ -70,6 +70,43 @@ __global__ void dsa_scores_kernel(const __nv_bfloat16* __restrict__ qi, int q_ld
   scores[(size_t)row * s_ld + key] = s;
 }
 
+// Head reduction after the tensor-core indexer GEMM. g [rows * H, g_ld] bf16 holds
+// q_h(t) . k(s) for the rows of one sequence segment (head-minor) over its first S
+// keys; scores[r][s] = sum_h w[r][h] relu(g[r H + h][s]) for s < ctx_r, -inf for
+// ctx_r <= s < s_ld. grid (ceil(s_ld / 1024), rows), 128 threads x 8 keys.
+__global__ void __launch_bounds__(128) dsa_head_reduce_kernel(const __nv_bfloat16* __restrict__ g, int g_ld, int S,
+                                                               const float* __restrict__ w, int w_ld, int H,
+                                                               const int* __restrict__ row_ctx,
+                                                               float* __restrict__ scores, int s_ld) {
+  const int r = blockIdx.y;
+  const int s0 = (blockIdx.x * 128 + threadIdx.x) * 8;
+  if (s0 >= s_ld) return;
+  const int ctx = min(row_ctx[r], S);
+  float wr[DSA_MAX_HEADS];
+#pragma unroll
+  for (int h = 0; h < DSA_MAX_HEADS; ++h) wr[h] = h < H ? w[(size_t)r * w_ld + h] : 0.f;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (s0 + 8 <= S) {
+#pragma unroll
+    for (int h = 0; h < DSA_MAX_HEADS; ++h) {
+      if (h >= H) break;
+      const uint4 u = *reinterpret_cast<const uint4*>(g + ((size_t)r * H + h) * g_ld + s0);
+      const float v[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
+                          bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += wr[h] * fmaxf(v[j], 0.f);
+    }
+  } else {
+    for (int h = 0; h < H; ++h)
+      for (int j = 0; j < 8 && s0 + j < S; ++j)
+        acc[j] += wr[h] * fmaxf(__bfloat162float(g[((size_t)r * H + h) * g_ld + s0 + j]), 0.f);
+  }
+  float* out = scores + (size_t)r * s_ld + s0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (s0 + j < s_ld) out[j] = s0 + j < ctx ? acc[j] : -INFINITY;
+}
+
 __device__ __forceinline__ uint32_t fkey(float f) {
   const uint32_t b = __float_as_uint(f);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -282,6 +319,27 @@ void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor 
       reinterpret_cast<const __nv_bfloat16*>(icache.data_ptr()), bt.data_ptr<int>(), bt.size(1),
       row_seq.data_ptr<int>(), row_ctx.data_ptr<int>(), scores.data_ptr<float>(), s_ld, icache.size(0),
       status.data_ptr<int>());
+  OM_LAUNCH_CHECK();
+}
+
+// scores [rows, s_ld] view (row stride s_ld); g [rows * H, >= S] bf16 from the indexer GEMM.
+void om_dsa_head_reduce(torch::Tensor g, int64_t S, torch::Tensor w, int64_t H, torch::Tensor row_ctx,
+                        torch::Tensor scores) {
+  const int rows = row_ctx.numel();
+  if (rows == 0) return;
+  TORCH_CHECK(H >= 1 && H <= om::DSA_MAX_HEADS, "dsa_head_reduce: 1..8 heads");
+  TORCH_CHECK(g.scalar_type() == at::kBFloat16 && g.stride(1) == 1 && g.size(0) == rows * H && g.size(1) >= S &&
+                  g.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(g.data_ptr()) & 15) == 0,
+              "dsa_head_reduce: g bf16 [rows * H, >= S], 16-byte aligned rows");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.size(0) == rows && scores.scalar_type() == at::kFloat &&
+                  scores.stride(1) == 1 && scores.stride(0) == scores.size(1) && scores.size(0) == rows &&
+                  row_ctx.scalar_type() == at::kInt,
+              "dsa_head_reduce: w fp32 [rows, H], scores fp32 [rows, s_ld], row_ctx int32");
+  const int s_ld = scores.size(1);
+  dim3 grid((s_ld + 1023) / 1024, rows);
+  om::dsa_head_reduce_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), g.stride(0), (int)S, w.data_ptr<float>(), w.stride(0),
+      (int)H, row_ctx.data_ptr<int>(), scores.data_ptr<float>(), scores.stride(0));
   OM_LAUNCH_CHECK();
 }
 

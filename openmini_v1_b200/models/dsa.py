@@ -113,8 +113,11 @@ def dsa_attention(model, i, L, a, qkv, fb, kv):
     if a.is_cuda:
         c = ops.ctx(a.device)
         scores = c.workspace("dsa_scores", T * s_ld)[:T * s_ld].view(T, s_ld)
-        _native.C().dsa_scores(qi, wi.contiguous(), d.indexer_heads, kv.idx_k[i], fb.block_tables, fb.row_seq,
-                               fb.row_ctx, scores, c.status)
+        if T >= TC_MIN_ROWS:
+            index_scores_tc(qi, wi.contiguous(), kv.idx_k[i], fb, d.indexer_heads, scores)
+        else:
+            _native.C().dsa_scores(qi, wi.contiguous(), d.indexer_heads, kv.idx_k[i], fb.block_tables, fb.row_seq,
+                                   fb.row_ctx, scores, c.status)
         sel = torch.empty(T, k, dtype=torch.int32, device=a.device)
         n = torch.empty(T, dtype=torch.int32, device=a.device)
         _native.C().dsa_topk(scores, fb.row_ctx, k, sel, n)
@@ -125,6 +128,41 @@ def dsa_attention(model, i, L, a, qkv, fb, kv):
     scores = index_scores_ref(qi, wi, kv.idx_k[i], fb.block_tables, fb.row_seq, fb.row_ctx, d.indexer_heads, s_ld)
     sel, n = topk_ref(scores, fb.row_ctx, k)
     return sparse_attention_ref(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, sel, n, model.hq, model.scale)
+
+
+TC_MIN_ROWS = 64          # prefill batches score on tensor cores; decode rows keep the bandwidth-bound kernel
+TC_MAX_GEMM_BYTES = 256 << 20
+
+
+def index_scores_tc(qi, wi, icache, fb, H: int, scores):
+    """Indexer scores of a prefill batch on tensor cores: per sequence segment of the
+    batch, its indexer keys are gathered contiguously ([S, 64], S rounded up to 64), the
+    tcgen05 GEMM computes every (row, head) dot product (q rows [n H, 64] x keys^T), and
+    ``dsa_head_reduce`` applies ReLU, the head weights and the causal mask into the
+    fp32 score rows. Rows are processed in chunks whose GEMM output stays under
+    ``TC_MAX_GEMM_BYTES``."""
+    Di = icache.shape[-1]
+    seq = fb.row_seq.cpu().tolist()
+    ctx = fb.row_ctx.cpu().tolist()
+    flat = icache.view(-1, Di)
+    T = len(seq)
+    r0 = 0
+    while r0 < T:
+        r1 = r0
+        while r1 < T and seq[r1] == seq[r0]:
+            r1 += 1
+        S = max(ctx[r0:r1])
+        Sp = (S + 63) // 64 * 64
+        pos = torch.arange(Sp, device=qi.device)
+        blk = fb.block_tables[seq[r0]].long()[(pos // 16).clamp(max=fb.block_tables.shape[1] - 1)]
+        keys = flat[(blk.clamp(min=0) * 16 + pos % 16).clamp(max=flat.shape[0] - 1)].contiguous()
+        step = max(1, TC_MAX_GEMM_BYTES // (H * Sp * 2))
+        for c0 in range(r0, r1, step):
+            c1 = min(r1, c0 + step)
+            q = qi[c0:c1].reshape((c1 - c0) * H, Di).contiguous()
+            g = ops.linear(q, keys)  # [rows * H, Sp] on the tcgen05 GEMM
+            _native.C().dsa_head_reduce(g, S, wi[c0:c1], H, fb.row_ctx[c0:c1], scores[c0:c1])
+        r0 = r1
 
 
 def _write_index(ki, slots, icache):

@@ -555,3 +555,32 @@ def test_mla_layer_gpu_matches_fp32():
     ops.check_status()
     want = mla_reference_layer(m, m.layers[0], a, fb.positions)
     _close(got, want, rtol=3e-2, atol=3e-2)
+
+
+def test_dsa_index_scores_tensor_core():
+    """Prefill indexer scores through the tcgen05 GEMM + head reduction against the fp32
+    statement: two sequence segments, one with a cached prefix (positions 300..449)."""
+    from types import SimpleNamespace
+    from openmini_v1_b200.models import dsa
+    H = 4
+    segs = [(0, 300, 150), (1, 0, 100)]  # (sequence, first position, rows)
+    rseq = torch.tensor([s for s, p, n in segs for _ in range(n)], dtype=torch.int32, device=DEV)
+    rctx = torch.tensor([p + i + 1 for s, p, n in segs for i in range(n)], dtype=torch.int32, device=DEV)
+    T = rseq.numel()
+    nb = 64
+    icache = _rand(nb, 16, 64, seed=80)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(2)).int().to(DEV)
+    bt = torch.stack([perm[:32], perm[32:]]).contiguous()
+    qi = _rand(T, H * 64, seed=81)
+    wi = torch.rand(T, H, device=DEV)
+    L = 450
+    scores = torch.empty(T, L, device=DEV)
+    fb = SimpleNamespace(row_seq=rseq, row_ctx=rctx, block_tables=bt)
+    dsa.index_scores_tc(qi, wi, icache, fb, H, scores)
+    torch.cuda.synchronize()
+    ops.check_status()
+    sref = dsa.index_scores_ref(qi.cpu(), wi.cpu(), icache.cpu(), bt.cpu(), rseq.cpu(), rctx.cpu(), H, L)
+    fin = torch.isfinite(sref)
+    assert torch.equal(torch.isfinite(scores.cpu()), fin)
+    err = (scores.cpu()[fin] - sref[fin]).abs()
+    assert float(err.max()) < 2e-2 * float(sref[fin].abs().max())
