@@ -56,7 +56,7 @@ def _pp_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _ep_worker(rank, world, port, q):
+def _ep_worker(rank, world, port, q, capacity=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -73,13 +73,15 @@ def _ep_worker(rank, world, port, q):
         want = full.logits(full(fb, full.allocate_kv(2)))
         par = ParallelState.build(ep=world)
         m = DecoderLM(cfg, device="cpu", seed=2)
-        m.set_ep(ExpertParallel(par.ep_group), par.ep_rank)
+        ep = ExpertParallel(par.ep_group, capacity_factor=capacity, max_tokens=32 if capacity else None)
+        m.set_ep(ep, par.ep_rank)
         assert len(m.layers[0]["experts_gate_up"]) == 4 // world
         fb2 = _batch(T)
         fb2.record_routing = {}
         got = m.logits(m(fb2, m.allocate_kv(2)))
         same_routing = all(torch.equal(fb.record_routing[i], fb2.record_routing[i]) for i in fb.record_routing)
-        q.put((rank, float((got - want).abs().max()), same_routing))
+        dropped = int(ep.dropped) if ep.dropped is not None else 0
+        q.put((rank, float((got - want).abs().max()), same_routing, dropped))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -108,9 +110,26 @@ def test_pipeline_parallel_matches_single_rank():
 
 
 def test_expert_parallel_matches_single_rank():
-    for rank, err, same in _run(_ep_worker):
+    for rank, err, same, _ in _run(_ep_worker):
         assert same
         assert err < 1e-4, (rank, err)
+
+
+def _ep_fixed_big(rank, world, port, q):
+    _ep_worker(rank, world, port, q, capacity=2.0)
+
+
+def _ep_fixed_small(rank, world, port, q):
+    _ep_worker(rank, world, port, q, capacity=0.25)
+
+
+def test_expert_parallel_fixed_capacity():
+    """Equal-split dispatch without host synchronisation: with room for every pair the
+    result equals one rank's; with a small capacity pairs are dropped and counted."""
+    for rank, err, same, dropped in _run(_ep_fixed_big):
+        assert same and dropped == 0 and err < 1e-4, (rank, err, dropped)
+    res = _run(_ep_fixed_small)
+    assert sum(r[3] for r in res) > 0
 
 
 def _tp_sample_worker(rank, world, port, q):
