@@ -105,3 +105,64 @@ def test_sp_transport_matches_allreduce(wfmt, push):
         assert not isinstance(mag, str), (rank, mag)
         assert max(errs) < 0.02 * max(mag, 1.0), (rank, errs, mag)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _ep_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from openmini_v1_b200 import ops
+        from openmini_v1_b200.models.config import ModelConfig, MoEConfig
+        from openmini_v1_b200.models.llama import DecoderLM, ForwardBatch
+        from openmini_v1_b200.parallel.expert import ExpertParallel
+        from openmini_v1_b200.parallel.state import ParallelState
+        dev = torch.device("cuda", rank)
+        cfg = ModelConfig(name="ep-test", vocab_size=1024, hidden_size=512, num_layers=2, num_heads=4,
+                          num_kv_heads=2, head_dim=128, intermediate_size=512,
+                          moe=MoEConfig(num_experts=2 * world, top_k=2, expert_ffn=256))
+        T = 40 + 8 * rank
+        i32 = dict(dtype=torch.int32, device=dev)
+        fb = lambda: ForwardBatch(torch.arange(3, 3 + T, **i32), torch.arange(T, **i32), torch.arange(T, **i32),  # noqa
+                                  torch.arange(4, **i32)[None], torch.zeros(T, **i32), torch.arange(1, T + 1, **i32),
+                                  T, torch.arange(T, device=dev))
+        full = DecoderLM(cfg, device=dev, seed=4)
+        want = full.logits(full(fb(), full.allocate_kv(4))).float()
+        m = DecoderLM(cfg, device=dev, seed=4)
+        ep = ExpertParallel(ParallelState.build(ep=world).ep_group, capacity_factor=float(world), max_tokens=64)
+        m.set_ep(ep, rank)
+        got = m.logits(m(fb(), m.allocate_kv(4))).float()
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        q.put((rank, [float((got - want).abs().max()) / max(1.0, float(want.abs().max()))], int(ep.dropped)))
+        dist.barrier()
+    except BaseException as e:
+        q.put((rank, [float("inf")], repr(e)))
+    sys.stdout.flush()
+    os._exit(0)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_fixed_capacity_on_gpus():
+    """Fixed-capacity expert parallelism over NCCL (grouped tcgen05 GEMMs for the local
+    experts) gives the single-GPU MoE result when nothing is dropped."""
+    world = min(torch.cuda.device_count(), 8)
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    finally:
+        for p in procs:
+            p.join(60)
+            if p.exitcode is None:
+                p.kill()
+                p.join(10)
+    for rank, errs, dropped in res:
+        assert not isinstance(dropped, str), (rank, dropped)
+        assert dropped == 0 and errs[0] < 3e-2, (rank, errs, dropped)
