@@ -154,6 +154,38 @@ def case_sample(batch, vocab):
 
 
 # name -> (builder, kwargs); the "all" sweep. Shapes are those of the 70B-shape decoder.
+def case_mla_decode(batch, ctx, heads):
+    """Absorbed MLA decode over a paged 576-wide latent cache (csrc/attn/mla.cu)."""
+    nb = batch * ((ctx + 15) // 16) + 4
+    cache = _rand(nb, 16, 576)
+    perm = torch.randperm(nb, device="cuda").to(torch.int32)
+    mb = (ctx + 15) // 16
+    bt = perm[: batch * mb].view(batch, mb).contiguous()
+    q = _rand(batch, heads, 576)
+    rseq = torch.arange(batch, dtype=torch.int32, device="cuda")
+    rctx = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty(batch, heads, 512, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: ops.mla_decode(q, cache, bt, rseq, rctx, ctx, 1 / math.sqrt(192), out=out)  # noqa
+    return fn, batch * ctx * 576 * 2 + q.numel() * 2 + out.numel() * 2, 2.0 * batch * heads * ctx * (576 + 512)
+
+
+def case_dsa_index_tc(rows, keys, heads=4):
+    """DSA prefill indexer scores on tensor cores: one sequence, rows ending at position keys."""
+    from types import SimpleNamespace
+    from ..models.dsa import index_scores_tc
+    nb = (keys + 15) // 16 + 2
+    icache = _rand(nb, 16, 64)
+    bt = torch.randperm(nb, device="cuda").to(torch.int32)[None, : (keys + 15) // 16].contiguous()
+    qi = _rand(rows, heads * 64)
+    wi = torch.rand(rows, heads, device="cuda")
+    fb = SimpleNamespace(row_seq=torch.zeros(rows, dtype=torch.int32, device="cuda"),
+                         row_ctx=torch.arange(keys - rows + 1, keys + 1, dtype=torch.int32, device="cuda"),
+                         block_tables=bt)
+    scores = torch.empty(rows, keys, device="cuda")
+    fn = lambda: index_scores_tc(qi, wi, icache, fb, heads, scores)  # noqa
+    return fn, rows * keys * 4 + keys * 128, 2.0 * rows * heads * keys * 64
+
+
 SUITE = {
     "gemm_bf16_decode_qkv": (case_gemm, dict(m=32, n=10240, k=8192, kind="bf16")),
     "gemm_q4_decode_qkv": (case_gemm, dict(m=32, n=10240, k=8192, kind="q4")),
@@ -171,6 +203,8 @@ SUITE = {
     "attn_prefill_tc": (case_prefill_attn, dict(seqs=4, seqlen=4096, hq=64, hkv=8)),
     "rmsnorm_residual": (case_rmsnorm, dict(rows=16384, dim=8192)),
     "sampler_topp_mask": (case_sample, dict(batch=256, vocab=128256)),
+    "mla_decode": (case_mla_decode, dict(batch=32, ctx=4096, heads=128)),
+    "dsa_index_tc_prefill": (case_dsa_index_tc, dict(rows=4096, keys=32768)),
 }
 
 
