@@ -49,7 +49,7 @@ class EngineConfig:
     seed: int = 0
     speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
     draft_engine: object = None            # with speculative_k: an LLMEngine of a draft model proposes instead
-    mtp_head: object = None                # with speculative_k: a models.mtp.MTPHead proposes the drafts
+    mtp_head: object = None                # with speculative_k: a models.mtp.MTPHead or CALMChunkHead proposes
     preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)
 
 
@@ -108,8 +108,10 @@ class LLMEngine:
         if self.cfg.speculative_k > 0:
             from .speculative import DraftModelProposer, NgramProposer
             if self.cfg.mtp_head is not None:
-                from ..models.mtp import MTPProposer
-                self.spec = MTPProposer(self.cfg.mtp_head, self.cfg.speculative_k)
+                from ..models.mtp import CALMChunkHead, CALMProposer, MTPProposer
+                h = self.cfg.mtp_head
+                self.spec = (CALMProposer(h, self.cfg.speculative_k) if isinstance(h, CALMChunkHead)
+                             else MTPProposer(h, self.cfg.speculative_k))
             else:
                 self.spec = (DraftModelProposer(self.cfg.draft_engine, self.cfg.speculative_k)
                              if self.cfg.draft_engine is not None else NgramProposer(self.cfg.speculative_k))

@@ -132,3 +132,86 @@ def train_mtp(head: MTPHead, sequences: list, steps: int = 100, lr: float = 1e-3
         losses.append(float(loss.detach()))
     head.p = {k: params[k].detach().to(orig[k].dtype) for k in orig}
     return losses
+
+
+class CALMChunkHead:
+    """Chunk-level generation (CALM): from the final hidden state h_t, K parallel heads
+    predict the tokens t+1 .. t+K in one step (head i: W_i RMSNorm(h) added to h, then
+    the shared LM head). A chunk is cut at the first token whose probability falls below
+    ``confidence``; as a proposer the verified speculative step keeps the output equal to
+    greedy decoding. Reference counterpart: openmini-server/src/model/inference/calm.rs
+    (hidden state -> multi-token chunk with a confidence gate)."""
+
+    def __init__(self, model, k: int = 4, confidence: float = 0.5, seed: int = 0, std: float = 0.02):
+        D = model.cfg.hidden_size
+        g = torch.Generator().manual_seed(seed)
+        self.model, self.k, self.confidence = model, k, confidence
+        self.w = [(torch.randn(D, D, generator=g) * std).to(model.device, model.dtype) for _ in range(k)]
+        self.eps = model.cfg.rms_eps
+
+    def chunk(self, h: torch.Tensor):
+        """h [D] -> (tokens, probabilities) of the confident prefix of the chunk."""
+        m = self.model
+        toks, probs = [], []
+        hn = ops.rmsnorm(h[None].contiguous(), m.norm, self.eps)
+        for W in self.w:
+            z = ops.linear(hn, W, resid=h[None].contiguous())
+            p = torch.softmax(m.logits(ops.rmsnorm(z, m.norm, self.eps)).float(), -1)[0]
+            pr, t = p.max(-1)
+            if float(pr) < self.confidence:
+                break
+            toks.append(int(t))
+            probs.append(float(pr))
+        return toks, probs
+
+    def train(self, sequences: list, steps: int = 100, lr: float = 1e-3) -> list:
+        """Fit head i to predict x_{t+1+i} from h_t of the main model (teacher forcing)."""
+        from .llama import ForwardBatch
+        m = self.model
+        dev = m.device
+        H, Y = [], []
+        with torch.no_grad():
+            for s in sequences:
+                T = len(s)
+                i32 = dict(dtype=torch.int32, device=dev)
+                nb = (T + 15) // 16
+                fb = ForwardBatch(torch.tensor(s, **i32), torch.arange(T, **i32), torch.arange(T, **i32),
+                                  torch.arange(nb, **i32)[None], torch.zeros(T, **i32),
+                                  torch.arange(1, T + 1, **i32), T, torch.arange(T, device=dev))
+                h = m(fb, m.allocate_kv(nb)).float()
+                n = T - self.k
+                H.append(h[:n])
+                Y.append(torch.stack([torch.tensor(s[1 + i:1 + i + n], device=dev) for i in range(self.k)], 1))
+        h, y = torch.cat(H), torch.cat(Y)
+        ws = [w.detach().float().clone().requires_grad_(True) for w in self.w]
+        opt = torch.optim.Adam(ws, lr=lr)
+        norm, head = m.norm.float(), m.lm_head.float()
+        rms = lambda x: x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * norm  # noqa: E731
+        losses = []
+        for _ in range(steps):
+            loss = sum(F.cross_entropy(rms(h + rms(h) @ W.t()) @ head.t(), y[:, i].long()) for i, W in enumerate(ws))
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+            losses.append(float(loss.detach()) / self.k)
+        self.w = [w.detach().to(m.dtype) for w in ws]
+        return losses
+
+
+class CALMProposer(MTPProposer):
+    """Speculative proposer from a CALM chunk head (drafts = the confident chunk)."""
+
+    def __init__(self, head: CALMChunkHead, k: int | None = None):
+        super().__init__(None, k or head.k)
+        self.calm = head
+
+    @torch.no_grad()
+    def propose(self, toks, k: int | None = None, req=None) -> list:
+        k = self.k if k is None else k
+        st = self.state.get(req.request_id) if req is not None else None
+        if k <= 0 or st is None or st[2] != len(toks):
+            return []
+        # the chunk head predicts from h behind the last token; its first draft is the
+        # token after the one just emitted, so the chunk is shifted by one
+        drafts, _ = self.calm.chunk(st[0])
+        return drafts[1:1 + k] if drafts and drafts[0] == st[1] else []

@@ -30,3 +30,21 @@ def test_mtp_speculative_equals_greedy_and_accepts():
     out = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=40, ignore_eos=True))[0]
     assert out.output_token_ids == ref
     assert eng.stats["spec_accepted"] > 0 and eng.stats["steps"] < 40
+
+
+def test_calm_chunk_proposer():
+    from openmini_v1_b200.models.mtp import CALMChunkHead
+    cfg = tiny()
+    cfg.num_layers = 1
+    cfg.vocab_size = 512
+    m = DecoderLM(cfg, device="cpu", seed=6)
+    prompt = [7, 8, 9]
+    ref = _greedy(m, prompt, 30)
+    head = CALMChunkHead(m, k=4, confidence=0.1, seed=2)  # random-init LM head: flat distributions
+    losses = head.train([prompt + ref], steps=200, lr=3e-3)
+    assert losses[-1] < losses[0] * 0.5
+    eng = LLMEngine(m, EngineConfig(max_num_seqs=2, max_model_len=256, use_cuda_graph=False, speculative_k=3,
+                                    mtp_head=head))
+    out = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=30, ignore_eos=True))[0]
+    assert out.output_token_ids == ref
+    assert eng.stats["spec_accepted"] > 0
