@@ -159,7 +159,8 @@ def main():
     max_len = a.prompt_max + a.out_tokens
     t_init = time.monotonic()
     model = DecoderLM(cfg, par=par, device=dev, seed=a.seed, weight_format=a.quant)
-    attach_tp_transport(model, par, dev, a.tp_transport, max_rows=4096)
+    # the fused transport covers whole prefill chunks (max_num_batched_tokens), not only decode
+    attach_tp_transport(model, par, dev, a.tp_transport, max_rows=16384)
     torch.cuda.synchronize()
     init_s = time.monotonic() - t_init
     eng = LLMEngine(model, EngineConfig(max_num_seqs=B, max_num_batched_tokens=16384, max_model_len=max_len,

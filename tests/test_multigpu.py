@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, wfmt, push):
+def _worker(rank, world, port, q, wfmt, push, T=37):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -41,14 +41,14 @@ def _worker(rank, world, port, q, wfmt, push):
                           num_kv_heads=2, head_dim=128, intermediate_size=2048)
         m = DecoderLM(cfg, par=par, device=dev, seed=3, weight_format=wfmt)
         m.set_comm(CollectiveOps(par.tp_group))
-        T = 37
         i32 = dict(dtype=torch.int32, device=dev)
         toks = torch.arange(5, 5 + T, **i32)
-        fb = ForwardBatch(toks, torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(4, **i32)[None],
+        nb = (T + 15) // 16
+        fb = ForwardBatch(toks, torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(nb, **i32)[None],
                           torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T, torch.arange(T, device=dev))
-        kv = m.allocate_kv(4)
+        kv = m.allocate_kv(nb)
         base = m.logits(m(fb, kv)).float()
-        m.set_sp(make_sp(par, dev, 256, cfg.hidden_size, push=push))
+        m.set_sp(make_sp(par, dev, 512, cfg.hidden_size, push=push))
         errs = []
         for _ in range(3):
             errs.append(float((m.logits(m(fb, kv)).float() - base).abs().max()))
@@ -78,9 +78,10 @@ def _worker(rank, world, port, q, wfmt, push):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("wfmt,push", [("bf16", True), ("bf16", False), ("q4", True), ("q4", False),
-                                       ("int8", False)])
-def test_sp_transport_matches_allreduce(wfmt, push):
+@pytest.mark.parametrize("wfmt,push,T", [("bf16", True, 37), ("bf16", False, 37), ("q4", True, 37),
+                                         ("q4", False, 37), ("int8", False, 37), ("q4", False, 300),
+                                         ("bf16", False, 300)])
+def test_sp_transport_matches_allreduce(wfmt, push, T):
     """push=True: the row-parallel GEMMs store their output tiles into the owner ranks'
     partials slots over NVLink and publish the epoch themselves (fused GEMM ->
     reduce-scatter); push=False (the default): local partials pulled by the reduce kernel,
@@ -90,7 +91,7 @@ def test_sp_transport_matches_allreduce(wfmt, push):
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, wfmt, push)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, wfmt, push, T)) for r in range(world)]
     for p in procs:
         p.start()
     try:
