@@ -40,6 +40,7 @@ void om_quantize_q4(torch::Tensor w, torch::Tensor q, torch::Tensor scales, c10:
 void om_dequant_q4(torch::Tensor q, torch::Tensor scales, torch::Tensor out);
 void om_quantize_int8(torch::Tensor w, torch::Tensor q, torch::Tensor scale);
 void om_dequant_int8(torch::Tensor q, torch::Tensor scale, torch::Tensor out);
+void om_gguf_dequant(torch::Tensor raw, int64_t type, torch::Tensor out);
 
 void om_dsa_scores(torch::Tensor qi, torch::Tensor wi, int64_t H, torch::Tensor icache, torch::Tensor bt,
                    torch::Tensor row_seq, torch::Tensor row_ctx, torch::Tensor scores, torch::Tensor status);
@@ -115,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequant_q4", &om_dequant_q4);
   m.def("quantize_int8", &om_quantize_int8);
   m.def("dequant_int8", &om_dequant_int8);
+  m.def("gguf_dequant", &om_gguf_dequant, "GGUF Q4_0 / Q8_0 / Q4_K / Q5_K / Q6_K blocks -> bf16 on the device");
   m.def("dsa_scores", &om_dsa_scores, "DSA indexer scores over the paged indexer-key cache");
   m.def("dsa_topk", &om_dsa_topk, "per-row top-k key positions");
   m.def("dsa_head_reduce", &om_dsa_head_reduce, "indexer scores from the tensor-core head GEMM: relu, weights, mask");

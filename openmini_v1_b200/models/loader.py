@@ -66,6 +66,13 @@ def _rows(t, lo, hi):
     return t[lo:hi]
 
 
+def _dense(t, model) -> torch.Tensor:
+    """The whole GGUF tensor dequantised on the model's device (GPU kernels for the
+    common block formats, host readers otherwise)."""
+    from ..gguf.device import dequantize_to_device
+    return dequantize_to_device(t.raw, t.type, tuple(t.shape), model.device, model.dtype)
+
+
 def _load_linear(src: _Src, t, model: DecoderLM, row_slice=None, col_slice=None):
     """Return a device weight for GGUF tensor ``t`` [N, K], sliced for tensor parallelism."""
     fmt = model.weight_format
@@ -87,7 +94,7 @@ def _load_linear(src: _Src, t, model: DecoderLM, row_slice=None, col_slice=None)
             from .quantize import tile_i8
             qd = torch.from_numpy(np.ascontiguousarray(q)).to(model.device)
             return Int8Weight(tile_i8(qd), torch.from_numpy(s.astype(np.float32)).to(model.device), qd.shape)
-    w = torch.from_numpy(np.ascontiguousarray(t.to_numpy()[r0:r1, c0:c1])).to(model.dtype).to(model.device)
+    w = _dense(t, model)[r0:r1, c0:c1].contiguous()
     if fmt == "q4":
         return Q4Weight.from_dense(w)
     if fmt == "int8":
@@ -106,11 +113,10 @@ def load_gguf_model(path: str, device="cpu", par=None, weight_format="bf16", dty
     hd = cfg.head_dim
 
     def dense(name, i=None, rows=None):
-        t = src.get(name, i)
-        a = t.to_numpy()
+        a = _dense(src.get(name, i), model)
         if rows:
             a = a[rows[0]:rows[1]]
-        return torch.from_numpy(np.ascontiguousarray(a)).to(model.dtype).to(model.device)
+        return a.contiguous()
 
     model.embed = dense("token_embd.weight")
     model.norm = dense("output_norm.weight")

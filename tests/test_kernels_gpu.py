@@ -584,3 +584,24 @@ def test_dsa_index_scores_tensor_core():
     assert torch.equal(torch.isfinite(scores.cpu()), fin)
     err = (scores.cpu()[fin] - sref[fin]).abs()
     assert float(err.max()) < 2e-2 * float(sref[fin].abs().max())
+
+
+@pytest.mark.parametrize("typ", [2, 8, 12, 13, 14])
+def test_gguf_device_dequant(typ):
+    """GGUF blocks expanded on the GPU equal the host readers (bf16 rounding of the result)."""
+    import numpy as np
+    from openmini_v1_b200.gguf.constants import BLOCK_SIZES, GGMLType
+    from openmini_v1_b200.gguf.device import dequantize_to_device
+    from openmini_v1_b200.gguf.quants import dequantize
+    per, nbytes = BLOCK_SIZES[GGMLType(typ)]
+    nblk = 64
+    rng = np.random.default_rng(typ)
+    b = rng.integers(0, 256, size=(nblk, nbytes), dtype=np.uint8)
+    f16_at = {2: (0,), 8: (0,), 12: (0, 2), 13: (0, 2), 14: (208,)}[typ]
+    for off in f16_at:
+        b[:, off:off + 2] = np.frombuffer(rng.uniform(-0.1, 0.1, nblk).astype(np.float16).tobytes(),
+                                          np.uint8).reshape(nblk, 2)
+    want = torch.from_numpy(dequantize(b.reshape(-1), typ, nblk * per)).view(4, -1)
+    got = dequantize_to_device(b.reshape(-1), typ, (4, nblk * per // 4), DEV)
+    # fp32 products on both sides; a fused multiply-add may move the bf16 rounding by one step
+    torch.testing.assert_close(got.float().cpu(), want.to(torch.bfloat16).float(), rtol=8e-3, atol=1e-6)
