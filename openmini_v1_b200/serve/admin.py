@@ -106,6 +106,7 @@ class AdminService:
         self.ttl = token_ttl_s
         self.sla = SLAMonitor()
         self.hooks = {}  # "model_status", "model_reload", "sessions", "metrics", "config", "service_action"
+        self.oidc = None  # serve.oidc.OIDCVerifier: bearer JWTs from an identity provider
         if bootstrap_admin and not self.store.q("SELECT 1 FROM users"):
             self.create_user(*bootstrap_admin, role="admin", actor="bootstrap")
 
@@ -170,11 +171,25 @@ class AdminService:
                 fired.append({"id": aid, "name": name, "metric": metric, "value": v, "threshold": thr})
         return fired
 
+    def _oidc_principal(self, tok: str):
+        from .oidc import OIDCError
+        try:
+            claims = self.oidc.verify(tok)
+        except OIDCError:
+            return None
+        role = self.oidc.role_of(claims)
+        if role is None:
+            return None
+        return Principal(claims.get("preferred_username") or claims.get("email") or claims.get("sub", "oidc"), role)
+
     # ------------------------------------------------------------------ HTTP
     def principal(self, authorization: str | None = Header(None), x_api_key: str | None = Header(None)):
         p = None
         if authorization and authorization.lower().startswith("bearer "):
-            p = self.verify_token(authorization[7:])
+            tok = authorization[7:]
+            p = self.verify_token(tok)
+            if p is None and self.oidc is not None and tok.count(".") == 2:
+                p = self._oidc_principal(tok)
         elif x_api_key:
             p = self.check_apikey(x_api_key)
         if p is None:

@@ -85,3 +85,50 @@ def test_admin_web_console_served_and_wired():
     tok = c.post("/admin/auth/login", json={"username": "admin", "password": "admin"}).json()["token"]
     for view in re.findall(r'data-view="([a-z]+)"', html):
         assert c.get(f"/admin/{view}", headers={"Authorization": f"Bearer {tok}"}).status_code == 200, view
+
+
+def _jwt(key, alg, claims, kid="k1"):
+    import json
+    from cryptography.hazmat.primitives import hashes
+    from cryptography.hazmat.primitives.asymmetric import ec, padding
+    from cryptography.hazmat.primitives.asymmetric.utils import decode_dss_signature
+    from openmini_v1_b200.serve.oidc import b64url_encode
+    h = b64url_encode(json.dumps({"alg": alg, "kid": kid, "typ": "JWT"}).encode())
+    p = b64url_encode(json.dumps(claims).encode())
+    msg = f"{h}.{p}".encode()
+    if alg == "RS256":
+        sig = key.sign(msg, padding.PKCS1v15(), hashes.SHA256())
+    else:
+        r, s = decode_dss_signature(key.sign(msg, ec.ECDSA(hashes.SHA256())))
+        sig = r.to_bytes(32, "big") + s.to_bytes(32, "big")
+    return f"{h}.{p}.{b64url_encode(sig)}"
+
+
+def test_oidc_bearer_tokens():
+    import time
+    from cryptography.hazmat.primitives.asymmetric import ec, rsa
+    from openmini_v1_b200.serve.oidc import OIDCVerifier, b64url_encode
+    rk = rsa.generate_private_key(public_exponent=65537, key_size=2048)
+    ek = ec.generate_private_key(ec.SECP256R1())
+    rn, en = rk.public_key().public_numbers(), ek.public_key().public_numbers()
+    b = lambda i, n: b64url_encode(i.to_bytes(n, "big"))  # noqa: E731
+    jwks = {"keys": [{"kty": "RSA", "kid": "k1", "n": b(rn.n, 256), "e": b(rn.e, 3)},
+                     {"kty": "EC", "crv": "P-256", "kid": "k2", "x": b(en.x, 32), "y": b(en.y, 32)}]}
+    svc = AdminService(secret=b"k" * 32)
+    svc.oidc = OIDCVerifier("https://idp.example", "openmini", jwks=jwks, role_map={"ops-team": "operator"})
+    app = FastAPI()
+    svc.mount(app)
+    c = TestClient(app)
+    now = time.time()
+    good = {"iss": "https://idp.example", "aud": "openmini", "exp": now + 60, "sub": "u1",
+            "preferred_username": "alice", "groups": ["eng", "ops-team"]}
+    for key, alg, kid in ((rk, "RS256", "k1"), (ek, "ES256", "k2")):
+        t = _jwt(key, alg, good, kid)
+        assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {t}"}).json() == \
+            {"user": "alice", "role": "operator"}
+    bad = [dict(good, exp=now - 100), dict(good, aud="other"), dict(good, iss="evil"), dict(good, groups=["eng"])]
+    for claims in bad:
+        t = _jwt(rk, "RS256", claims)
+        assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {t}"}).status_code == 401, claims
+    forged = _jwt(rsa.generate_private_key(public_exponent=65537, key_size=2048), "RS256", good)
+    assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {forged}"}).status_code == 401
