@@ -5,9 +5,9 @@ Behaviour of the reference's OpenMiniService
 from the session's stored memory plus the request messages ("role: content"
 lines) and streams one ChatResponse per generated token, finishing with usage;
 HealthCheck reports engine state. ImageUnderstanding(-Stream) run the vision
-encoder and the engine when the server was started with one (``vision``);
-otherwise they, and the speech RPCs, answer UNIMPLEMENTED instead of synthetic
-output.
+encoder and SpeechToText the audio encoder, then the engine, when the server was
+started with them (``vision``, ``speech``); otherwise they, and TextToSpeech (no
+vocoder), answer UNIMPLEMENTED instead of synthetic output.
 Session memory is kept in SQLite (the reference's database), see ``SessionStore``.
 """
 from __future__ import annotations
@@ -55,8 +55,9 @@ class SessionStore:
 
 class OpenMiniServicer:
     def __init__(self, aengine, tokenizer, store: SessionStore | None = None, metrics=None, default_max_tokens=256,
-                 vision=None):
+                 vision=None, speech=None):
         self.vision = vision
+        self.speech = speech
         self.aengine = aengine
         self.tok = tokenizer
         self.store = store or SessionStore()
@@ -110,6 +111,24 @@ class OpenMiniServicer:
                 yield proto.ImageResponse(session_id=request.session_id, token=piece, finished=fin)
         except Exception as e:
             await context.abort(grpc.StatusCode.INVALID_ARGUMENT, f"image: {e}")
+
+    async def SpeechToText(self, request_iterator, context):
+        """Client-streamed audio chunks (one clip); the transcript is streamed back."""
+        if self.speech is None:
+            await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no audio encoder loaded")
+        import math
+        chunks, sid, lang = [], "", ""
+        async for req in request_iterator:
+            chunks.append(req.audio_data)
+            sid, lang = req.session_id or sid, req.language or lang
+        try:
+            lps = []
+            async for piece, fin, lp in self.speech.stream(b"".join(chunks), lang):
+                lps.append(lp)
+                conf = math.exp(sum(lps) / len(lps)) if lps else 0.0
+                yield proto.SpeechToTextResponse(session_id=sid, text=piece, finished=fin, confidence=conf)
+        except Exception as e:
+            await context.abort(grpc.StatusCode.INVALID_ARGUMENT, f"audio: {e}")
 
     async def _unimplemented(self, request, context):
         await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no vision / speech encoder loaded")

@@ -44,7 +44,7 @@ def chat_prompt(messages) -> str:
 
 
 def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metrics | None = None,
-               config=None, trainer_factory=None, vision=None) -> FastAPI:
+               config=None, trainer_factory=None, vision=None, speech=None) -> FastAPI:
     app = FastAPI(title="openmini_v1_b200")
     metrics = metrics or Metrics()
     metrics.model_loaded.set(1)
@@ -276,7 +276,23 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
             return JSONResponse({"error": f"bad image request: {e}"}, status_code=400)
         return {"answer": text, "usage": {"prompt_tokens": pt, "completion_tokens": n, "total_tokens": pt + n}}
 
-    for path in ("/api/v1/tts", "/api/v1/stt"):
+    @app.post("/api/v1/stt")
+    async def stt(body: dict):
+        """{"audio": base64 WAV or .npy bytes, "language"?: str, "max_tokens"?: int}"""
+        if speech is None:
+            return JSONResponse({"error": "/api/v1/stt needs an audio encoder, which is not loaded"}, status_code=501)
+        import base64
+        try:
+            data = base64.b64decode(body["audio"])
+            text = []
+            async for piece, fin, lp in speech.stream(data, str(body.get("language", "")),
+                                                      int(body.get("max_tokens", 0))):
+                text.append(piece)
+        except (KeyError, ValueError, OSError, EOFError) as e:
+            return JSONResponse({"error": f"bad audio request: {e}"}, status_code=400)
+        return {"text": "".join(text), "tokens": len(text)}
+
+    for path in ("/api/v1/tts",):
         async def _ni(path=path):
             return JSONResponse({"error": f"{path} needs a vision / speech encoder, which is not loaded"},
                                 status_code=501)

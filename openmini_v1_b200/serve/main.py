@@ -77,12 +77,21 @@ async def serve(args):
         if eng.device.type == "cpu":
             vc.hidden_size, vc.num_layers, vc.mlp_size, vc.num_heads = 256, 2, 512, 2
         vision = ImageUnderstanding(aeng, tok, VisionEncoder(vc, device=eng.device, dtype=eng.model.dtype))
-    app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg, vision=vision)
+    speech = None
+    if args.audio:
+        from ..models.audio import AudioConfig, AudioEncoder
+        from .vision_service import SpeechToText
+        ac = AudioConfig(lm_hidden=eng.model.cfg.hidden_size)
+        if eng.device.type == "cpu":
+            ac.hidden_size, ac.num_layers, ac.mlp_size, ac.num_heads = 256, 2, 512, 2
+        speech = SpeechToText(aeng, tok, AudioEncoder(ac, device=eng.device, dtype=eng.model.dtype))
+    app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg, vision=vision,
+                     speech=speech)
     import uvicorn
     http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
                                          log_level="warning"))
     store = SessionStore(cfg.database.path if args.db else ":memory:")
-    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision),
+    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision, speech=speech),
                                                  f"{cfg.server.host}:{args.grpc_port or cfg.server.port}",
                                                  cfg.grpc.max_message_size_mb)
     gw = Gateway(aeng, tok, cfg.server.max_connections)
@@ -115,6 +124,8 @@ def main(argv=None):
     p.add_argument("--db", action="store_true", help="persist chat sessions to [database].path")
     p.add_argument("--vision", action="store_true",
                    help="load a vision encoder (random-init weights) and serve image understanding")
+    p.add_argument("--audio", action="store_true",
+                   help="load an audio encoder (random-init weights) and serve speech-to-text")
     args = p.parse_args(argv)
     init_logging()
     asyncio.run(serve(args))

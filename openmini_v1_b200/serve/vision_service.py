@@ -65,3 +65,31 @@ class ImageUnderstanding:
         async for piece, fin, pt, n in self.stream(image_bytes, question, max_tokens, temperature):
             text.append(piece)
         return "".join(text), pt, n
+
+
+class SpeechToText:
+    """Speech input: decode the audio, run the audio encoder, splice the features into a
+    transcription prompt (placeholder ids derived from the audio bytes, as for images)
+    and generate."""
+
+    def __init__(self, aengine, tokenizer, encoder, default_max_tokens: int = 128):
+        self.aengine, self.tok, self.enc = aengine, tokenizer, encoder
+        self.default_max = default_max_tokens
+        self.vocab = aengine.engine.model.cfg.vocab_size
+
+    def prepare(self, audio_bytes: bytes, language: str = ""):
+        from ..models.audio import decode_audio
+        feats = self.enc.encode(decode_audio(audio_bytes, self.enc.cfg.sample_rate))
+        head = self.tok.encode("user: <audio>\n")
+        tail = self.tok.encode(f"transcribe{(' (' + language + ')') if language else ''}:\nassistant:",
+                               add_bos=False)
+        return head + image_ids(audio_bytes, feats.shape[0], self.vocab) + tail, (len(head), feats)
+
+    async def stream(self, audio_bytes: bytes, language: str = "", max_tokens: int = 0):
+        ids, feats = self.prepare(audio_bytes, language)
+        sp = SamplingParams(temperature=0.0, max_tokens=max_tokens or self.default_max, logprobs=True)
+        dec, n = IncrementalDecoder(self.tok), 0
+        async for out in self.aengine.generate(ids, sp, image_embeds=feats):
+            n += 1
+            lp = out.logprobs[-1] if getattr(out, "logprobs", None) else 0.0
+            yield dec.push(out.new_token_ids[0]), out.finished, lp

@@ -96,3 +96,64 @@ def test_http_and_grpc_image_routes(vstack):
         finally:
             await server.stop(1)
     asyncio.run(run())
+
+
+def _wav(seconds=0.5, rate=22050, seed=0):
+    import wave
+    t = np.arange(int(seconds * rate)) / rate
+    x = 0.3 * np.sin(2 * np.pi * 440 * t) + 0.05 * np.random.default_rng(seed).normal(size=t.size)
+    b = io.BytesIO()
+    with wave.open(b, "wb") as w:
+        w.setnchannels(1)
+        w.setsampwidth(2)
+        w.setframerate(rate)
+        w.writeframes((x * 32767).astype(np.int16).tobytes())
+    return b.getvalue()
+
+
+def test_audio_features_and_speech_routes(vstack):
+    from openmini_v1_b200.models.audio import AudioConfig, AudioEncoder, decode_audio, log_mel, mel_filterbank
+    from openmini_v1_b200.serve.vision_service import SpeechToText
+    aeng, tok, m, vis = vstack
+    fb = mel_filterbank(16000, 400, 80)
+    freqs = torch.linspace(0, 8000, 201)
+    centre = (fb @ freqs) / fb.sum(1)  # filter centroids do not fall with the band index
+    assert fb.shape == (80, 201) and (fb >= 0).all() and bool((centre[1:] >= centre[:-1] - 1e-3).all()) and centre[-1] > 7000
+    wav = decode_audio(_wav(), 16000)
+    assert abs(wav.numel() - 8000) <= 1 and wav.abs().max() < 1.0
+    lm = log_mel(wav, AudioConfig())
+    assert lm.shape == (51, 80)
+    # the 440 Hz tone is the loudest band
+    assert abs(float(centre[int(lm.mean(0).argmax())]) - 440) < 100
+    enc = AudioEncoder(AudioConfig(hidden_size=128, num_layers=1, num_heads=2, mlp_size=256, lm_hidden=256),
+                       device="cpu", dtype=torch.float32)
+    feats = enc.encode(wav)
+    assert feats.shape == (26, 256) and torch.isfinite(feats).all()
+    stt = SpeechToText(aeng, tok, enc, default_max_tokens=3)
+    c = TestClient(create_app(aeng, tok, "tiny", speech=stt))
+    r = c.post("/api/v1/stt", json={"audio": base64.b64encode(_wav()).decode()})
+    assert r.status_code == 200 and r.json()["tokens"] == 3
+    assert TestClient(create_app(aeng, tok, "tiny")).post("/api/v1/stt", json={"audio": ""}).status_code == 501
+    import grpc
+    from openmini_v1_b200.serve import proto
+    from openmini_v1_b200.serve.grpc_server import OpenMiniServicer, start_grpc_server
+
+    async def run():
+        server, port = await start_grpc_server(OpenMiniServicer(aeng, tok, speech=stt), "127.0.0.1:0")
+        try:
+            async with grpc.aio.insecure_channel(f"127.0.0.1:{port}") as ch:
+                data = _wav(seed=1)
+                reqs = [proto.SpeechToTextRequest(session_id="a", audio_data=data[i:i + 4000])
+                        for i in range(0, len(data), 4000)]
+
+                async def gen():
+                    for q in reqs:
+                        yield q
+                call = ch.stream_stream(f"/{proto.SERVICE}/SpeechToText",
+                                        request_serializer=proto.message("SpeechToTextRequest").SerializeToString,
+                                        response_deserializer=proto.message("SpeechToTextResponse").FromString)
+                outs = [o async for o in call(gen())]
+                assert len(outs) == 3 and outs[-1].finished and 0 < outs[-1].confidence <= 1
+        finally:
+            await server.stop(1)
+    asyncio.run(run())
