@@ -169,6 +169,20 @@ class BlockManager {
     return out;
   }
 
+  // Decode batch: the cache slot of position pos[i] of sequence sids[i] -> out[i].
+  void decode_slots(const std::vector<int64_t>& sids, py::array_t<int32_t> pos, py::array_t<int32_t> out) const {
+    auto p = pos.unchecked<1>();
+    auto o = out.mutable_unchecked<1>();
+    if ((size_t)p.shape(0) < sids.size() || (size_t)o.shape(0) < sids.size())
+      throw std::out_of_range("decode_slots: arrays shorter than the batch");
+    for (size_t i = 0; i < sids.size(); ++i) {
+      const Seq& s = get(sids[i]);
+      const int t = p(i);
+      if (t < 0 || t >= (int)s.blocks.size() * bs_) throw std::out_of_range("decode_slots: position");
+      o(i) = s.blocks[t / bs_] * bs_ + (t % bs_);
+    }
+  }
+
   // Fill a [len(sids), max_blocks] int32 numpy array (padded with 0).
   void fill_block_tables(const std::vector<int64_t>& sids, py::array_t<int32_t> out) const {
     auto buf = out.mutable_unchecked<2>();
@@ -297,6 +311,7 @@ void bind_block_manager(py::module_& m) {
       .def("block_table", &BlockManager::block_table)
       .def("seq_len", &BlockManager::seq_len)
       .def("slots", &BlockManager::slots)
+      .def("decode_slots", &BlockManager::decode_slots)
       .def("fill_block_tables", &BlockManager::fill_block_tables)
       .def("prefix_hit_rate", &BlockManager::prefix_hit_rate)
       .def("ref_count", &BlockManager::ref_count)

@@ -336,7 +336,21 @@ class LLMEngine:
         o = 0
         logits_rows = []
         rows_req = []
-        for si, c in enumerate(chunks):
+        if so.kind == "decode" and T == S and all(c.wants_logits for c in chunks):
+            # one row per sequence: vectorised, the slots in one C++ call
+            reqs = [c.req for c in chunks]
+            p = np.fromiter((c.start for c in chunks), dtype=np.int32, count=S)
+            ids[:] = [c.req.token_slice(c.start, c.end)[0] for c in chunks]
+            pos[:] = p
+            self.bm.decode_slots([r.seq_id for r in reqs], p, slots)
+            rseq[:] = np.arange(S, dtype=np.int32)
+            rctx[:] = p + 1
+            logits_rows = list(range(S))
+            rows_req = reqs
+            chunks_loop = ()
+        else:
+            chunks_loop = chunks
+        for si, c in enumerate(chunks_loop):
             r = c.req
             n = c.end - c.start
             ids[o:o + n] = r.token_slice(c.start, c.end)
