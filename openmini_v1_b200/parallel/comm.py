@@ -154,3 +154,65 @@ class LocalComm:
 
     def barrier(self):
         self._exchange(None, lambda xs: None)
+
+
+# ----------------------------------------------------------------------------- backends + failover
+
+BACKENDS: dict = {}
+
+
+def register_backend(name: str, factory):
+    """``factory(**kw) -> object with the CollectiveOps interface``."""
+    BACKENDS[name] = factory
+
+
+def make_backend(name: str, **kw):
+    if name not in BACKENDS:
+        raise KeyError(f"unknown communication backend {name!r}; registered: {sorted(BACKENDS)}")
+    return BACKENDS[name](**kw)
+
+
+register_backend("nccl", lambda group=None: CollectiveOps(group))   # process group of the NCCL backend
+register_backend("gloo", lambda group=None: CollectiveOps(group))   # a gloo process group (CPU / control)
+register_backend("local", lambda rank, shared: LocalComm(rank, shared))
+
+
+class FailoverComm:
+    """Collectives over a primary backend that fall back to a secondary one (for example
+    NCCL over NVLink -> gloo over TCP) once the primary raises; the switch is sticky and
+    recorded. Every rank must fail over together, which holds when the primary fails on
+    all of them (a dead link or process group); ``on_failover(name, exc)`` lets the
+    caller notify the cluster control plane.
+
+    Reference counterpart: openmini-server/src/distributed/exo_communication.rs
+    (backend selection with failover between transports)."""
+
+    OPS = ("all_reduce", "all_gather", "reduce_scatter", "broadcast", "barrier", "all_to_all")
+
+    def __init__(self, primary, secondary, on_failover=None, names=("primary", "secondary")):
+        self.backends = [primary, secondary]
+        self.names = names
+        self.active = 0
+        self.failures: list = []
+        self.on_failover = on_failover
+
+    def _call(self, op, *a, **kw):
+        try:
+            return getattr(self.backends[self.active], op)(*a, **kw)
+        except Exception as e:
+            if self.active == 1:
+                raise
+            self.failures.append((op, repr(e)))
+            self.active = 1
+            if self.on_failover:
+                self.on_failover(self.names[1], e)
+            return getattr(self.backends[1], op)(*a, **kw)
+
+    def __getattr__(self, op):
+        if op in FailoverComm.OPS:
+            return lambda *a, **kw: self._call(op, *a, **kw)
+        raise AttributeError(op)
+
+    @property
+    def backend_name(self) -> str:
+        return self.names[self.active]

@@ -124,3 +124,34 @@ def test_local_comm_threads():
         t.join(30)
     for r in range(3):
         assert out[r][0] == 3.0 and out[r][1] == [0, 1, 2] and out[r][2] == [6.0, 6.0]
+
+
+def test_backend_registry_and_failover():
+    import threading
+    import torch
+    from openmini_v1_b200.parallel.comm import FailoverComm, LocalComm, make_backend
+
+    class Broken:
+        def all_reduce(self, t, op=None):
+            raise RuntimeError("NCCL watchdog: link down")
+
+    comms = LocalComm.create(2)
+    assert isinstance(make_backend("local", rank=0, shared=comms[0].shared), LocalComm)
+    events, out = [], [None, None]
+
+    def run(r):
+        fc = FailoverComm(Broken(), comms[r], on_failover=lambda n, e: events.append((r, n)),
+                          names=("nccl", "local"))
+        out[r] = (fc.all_reduce(torch.full((3,), float(r + 1))), fc.backend_name, list(fc.failures))
+    ts = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(10)
+    for r in range(2):
+        val, name, fails = out[r]
+        assert torch.equal(val, torch.full((3,), 3.0)) and name == "local" and fails[0][0] == "all_reduce"
+    assert sorted(events) == [(0, "local"), (1, "local")]
+    import pytest
+    with pytest.raises(KeyError):
+        make_backend("carrier-pigeon")
