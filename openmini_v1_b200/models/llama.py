@@ -195,7 +195,7 @@ class DecoderLM(nn.Module):
         self._sp = sp
 
     def _use_sp(self, T: int) -> bool:
-        return (self._sp is not None and self._sp.fits(T) and not self.cfg.dsa.enabled and not self.cfg.mla.enabled
+        return (self._sp is not None and self._sp.fits(T) and not self.cfg.mla.enabled
                 and self.cfg.sliding_window <= 0
                 and not any("router" in L for L in self.layers))
 
@@ -244,7 +244,10 @@ class DecoderLM(nn.Module):
             qkv = sp.linear_ag(x[:T], L["qkv"])
             ops.rope_kv(qkv, fb.positions, fb.slots, kv.k[i], kv.v[i], self.inv_freq, self.hq, self.hkv, self.hd,
                         cfg.rope_mode)
-            if fb.prefill_tiles is not None and self.hd == 128:
+            if cfg.dsa.enabled:  # the indexer reads the gathered rows the QKV GEMM waited for
+                from .dsa import dsa_attention
+                attn = dsa_attention(self, i, L, x[:T], qkv, fb, kv)
+            elif fb.prefill_tiles is not None and self.hd == 128:
                 attn = ops.flash_prefill(qkv, kv.k[i], kv.v[i], fb.block_tables, fb.row_seq, fb.row_ctx,
                                          fb.prefill_tiles, self.hq, self.scale)
             else:

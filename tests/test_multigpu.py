@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, wfmt, push, T=37):
+def _worker(rank, world, port, q, wfmt, push, T=37, dsa=False):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -37,8 +37,10 @@ def _worker(rank, world, port, q, wfmt, push, T=37):
         from openmini_v1_b200.parallel.symm import make_sp
         dev = torch.device("cuda", rank)
         par = ParallelState.build(tp=world)
+        from openmini_v1_b200.models.config import DSAConfig
         cfg = ModelConfig(name="tp-test", vocab_size=1024, hidden_size=1024, num_layers=3, num_heads=8,
-                          num_kv_heads=2, head_dim=128, intermediate_size=2048)
+                          num_kv_heads=2, head_dim=128, intermediate_size=2048,
+                          dsa=DSAConfig(enabled=dsa, top_k=16, threshold=8))
         m = DecoderLM(cfg, par=par, device=dev, seed=3, weight_format=wfmt)
         m.set_comm(CollectiveOps(par.tp_group))
         i32 = dict(dtype=torch.int32, device=dev)
@@ -78,10 +80,11 @@ def _worker(rank, world, port, q, wfmt, push, T=37):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("wfmt,push,T", [("bf16", True, 37), ("bf16", False, 37), ("q4", True, 37),
-                                         ("q4", False, 37), ("int8", False, 37), ("q4", False, 300),
-                                         ("bf16", False, 300)])
-def test_sp_transport_matches_allreduce(wfmt, push, T):
+@pytest.mark.parametrize("wfmt,push,T,dsa", [("bf16", True, 37, False), ("bf16", False, 37, False),
+                                             ("q4", True, 37, False), ("q4", False, 37, False),
+                                             ("int8", False, 37, False), ("q4", False, 300, False),
+                                             ("bf16", False, 300, False), ("q4", False, 37, True)])
+def test_sp_transport_matches_allreduce(wfmt, push, T, dsa):
     """push=True: the row-parallel GEMMs store their output tiles into the owner ranks'
     partials slots over NVLink and publish the epoch themselves (fused GEMM ->
     reduce-scatter); push=False (the default): local partials pulled by the reduce kernel,
@@ -91,7 +94,7 @@ def test_sp_transport_matches_allreduce(wfmt, push, T):
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, wfmt, push, T)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, wfmt, push, T, dsa)) for r in range(world)]
     for p in procs:
         p.start()
     try:
