@@ -170,3 +170,58 @@ def test_expert_parallel_fixed_capacity_on_gpus():
     for rank, errs, dropped in res:
         assert not isinstance(dropped, str), (rank, dropped)
         assert dropped == 0 and errs[0] < 3e-2, (rank, errs, dropped)
+
+
+def _ring_worker(rank, world, port, q):
+    import math
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from openmini_v1_b200 import ops
+        from openmini_v1_b200.parallel.ring_attention import attend, ring_attention
+        dev = torch.device("cuda", rank)
+        C, H, Hkv, D = 192, 8, 2, 128
+        g = torch.Generator(device=dev).manual_seed(11)  # the same full sequence on every rank
+        qf = torch.randn(world * C, H, D, generator=g, device=dev).to(torch.bfloat16)
+        kf = torch.randn(world * C, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        vf = torch.randn(world * C, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+        sl = slice(rank * C, (rank + 1) * C)
+        out, _ = ring_attention(qf[sl].contiguous(), kf[sl].contiguous(), vf[sl].contiguous(), 1 / math.sqrt(D))
+        full, _ = attend(qf, kf, vf, 1 / math.sqrt(D), causal=True)
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        err = float((out.float() - full[sl].float()).abs().max())
+        q.put((rank, [err], float(full.abs().max())))
+        dist.barrier()
+    except BaseException as e:
+        q.put((rank, [float("inf")], repr(e)))
+    sys.stdout.flush()
+    os._exit(0)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ring_context_parallel_on_gpus():
+    """Ring attention over NCCL point-to-point (each rank one contiguous chunk of a causal
+    sequence, chunks circulating while the previous one is attended) equals full
+    attention on one GPU."""
+    world = min(torch.cuda.device_count(), 8)
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    finally:
+        for p in procs:
+            p.join(60)
+            if p.exitcode is None:
+                p.kill()
+                p.join(10)
+    for rank, errs, mag in res:
+        assert not isinstance(mag, str), (rank, mag)
+        assert errs[0] < 2e-2 * max(mag, 1.0), (rank, errs, mag)
