@@ -55,6 +55,17 @@ export interface ImageAnswer {
   usage: Usage;
 }
 
+export interface SpeechAudio {
+  audio_data: string;   // base64 WAV (16-bit PCM mono)
+  sample_rate: number;
+  duration_s: number;
+}
+
+export interface Transcript {
+  text: string;
+  tokens: number;
+}
+
 export class OpenMiniError extends Error {
   constructor(public status: number, body: string) {
     super(`openmini HTTP ${status}: ${body}`);
@@ -129,6 +140,17 @@ export class OpenMiniClient {
     let bin = "";
     imageBytes.forEach((b) => (bin += String.fromCharCode(b)));
     return this.call("POST", "/api/v1/image/understand", { image: btoa(bin), question, max_tokens: maxTokens });
+  }
+
+  textToSpeech(text: string, opts: { voice?: string; language?: string; speed?: number; pitch?: number } = {}):
+      Promise<SpeechAudio> {
+    return this.call("POST", "/api/v1/tts", { text, ...opts });
+  }
+
+  speechToText(wavBytes: Uint8Array, language = "", maxTokens = 0): Promise<Transcript> {
+    let bin = "";
+    wavBytes.forEach((b) => (bin += String.fromCharCode(b)));
+    return this.call("POST", "/api/v1/stt", { audio: btoa(bin), language, max_tokens: maxTokens });
   }
 
   stats(): Promise<Record<string, unknown>> {

@@ -103,6 +103,37 @@ def _sinusoids(n: int, d: int) -> torch.Tensor:
     return torch.cat([a.sin(), a.cos()], 1)
 
 
+def attention_full(qkv: torch.Tensor, n: int, H: int, Dh: int) -> torch.Tensor:
+    """Bidirectional multi-head attention over ``n`` rows of a fused [n, 3 H Dh] QKV:
+    the FlashAttention kernel on the GPU when Dh is 128, fp32 softmax attention otherwise."""
+    if qkv.is_cuda and Dh == 128:
+        from ..parallel.ring_attention import attend
+        q, k, v = (qkv[:, i * H * Dh:(i + 1) * H * Dh].reshape(n, H, Dh).contiguous() for i in range(3))
+        out, _ = attend(q, k, v, 1 / math.sqrt(Dh), causal=False)
+        return out.to(qkv.dtype).reshape(n, H * Dh)
+    q, k, v = (qkv[:, i * H * Dh:(i + 1) * H * Dh].float().reshape(n, H, Dh).transpose(0, 1) for i in range(3))
+    p = torch.softmax(q @ k.transpose(1, 2) / math.sqrt(Dh), -1)
+    return (p @ v).transpose(0, 1).reshape(n, H * Dh).to(qkv.dtype)
+
+
+def init_blocks(n: int, D: int, mlp: int, rnd, one, zero) -> list:
+    """Weights of ``n`` pre-LayerNorm transformer blocks (``rnd(*shape)`` draws a weight)."""
+    return [{"ln1_w": one(), "ln1_b": zero(), "qkv": rnd(3 * D, D), "o": rnd(D, D),
+             "ln2_w": one(), "ln2_b": zero(), "fc1": rnd(mlp, D), "fc2": rnd(D, mlp)} for _ in range(n)]
+
+
+def run_blocks(x: torch.Tensor, layers: list, H: int, eps: float) -> torch.Tensor:
+    """Pre-LayerNorm blocks with bidirectional attention and a GELU MLP, residuals in fp32."""
+    n, D = x.shape
+    for L in layers:
+        a = ops.layernorm(x, L["ln1_w"], L["ln1_b"], eps)
+        att = attention_full(ops.linear(a, L["qkv"]), n, H, D // H)
+        x = (x.float() + ops.linear(att, L["o"]).float()).to(x.dtype)
+        m = ops.layernorm(x, L["ln2_w"], L["ln2_b"], eps)
+        x = (x.float() + ops.linear(ops.gelu(ops.linear(m, L["fc1"])), L["fc2"]).float()).to(x.dtype)
+    return x
+
+
 class AudioEncoder:
     def __init__(self, cfg: AudioConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0, std: float = 0.02):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
@@ -114,9 +145,7 @@ class AudioEncoder:
         self.conv1 = rnd(D, cfg.n_mels * 3)
         self.conv2 = rnd(D, D * 3)
         self.pos = _sinusoids(cfg.max_frames // 2 + 1, D).to(self.device, dtype)
-        self.layers = [{"ln1_w": one(), "ln1_b": zero(), "qkv": rnd(3 * D, D), "o": rnd(D, D),
-                        "ln2_w": one(), "ln2_b": zero(), "fc1": rnd(cfg.mlp_size, D), "fc2": rnd(D, cfg.mlp_size)}
-                       for _ in range(cfg.num_layers)]
+        self.layers = init_blocks(cfg.num_layers, D, cfg.mlp_size, rnd, one, zero)
         self.post_w, self.post_b = one(), zero()
         self.proj = rnd(cfg.lm_hidden, D)
 
@@ -127,17 +156,6 @@ class AudioEncoder:
         cols = xp.unfold(0, 3, stride)                                        # [T', C, 3]
         return ops.linear(cols.transpose(1, 2).reshape(cols.shape[0], -1).contiguous(), w)
 
-    def _attention(self, qkv, n):
-        H, Dh = self.cfg.num_heads, self.cfg.head_dim
-        if qkv.is_cuda and Dh == 128:
-            from ..parallel.ring_attention import attend
-            q, k, v = (qkv[:, i * H * Dh:(i + 1) * H * Dh].reshape(n, H, Dh).contiguous() for i in range(3))
-            out, _ = attend(q, k, v, 1 / math.sqrt(Dh), causal=False)
-            return out.to(qkv.dtype).reshape(n, H * Dh)
-        q, k, v = (qkv[:, i * H * Dh:(i + 1) * H * Dh].float().reshape(n, H, Dh).transpose(0, 1) for i in range(3))
-        p = torch.softmax(q @ k.transpose(1, 2) / math.sqrt(Dh), -1)
-        return (p @ v).transpose(0, 1).reshape(n, H * Dh).to(qkv.dtype)
-
     def encode(self, wav: torch.Tensor) -> torch.Tensor:
         """[samples] -> projected features [frames / 2, lm_hidden]."""
         cfg = self.cfg
@@ -146,11 +164,6 @@ class AudioEncoder:
         x = ops.gelu(self._conv(x, self.conv2, 2))
         n = x.shape[0]
         x = (x.float() + self.pos[:n].float()).to(self.dtype)
-        for L in self.layers:
-            a = ops.layernorm(x, L["ln1_w"], L["ln1_b"], cfg.ln_eps)
-            att = self._attention(ops.linear(a, L["qkv"]), n)
-            x = (x.float() + ops.linear(att, L["o"]).float()).to(self.dtype)
-            m = ops.layernorm(x, L["ln2_w"], L["ln2_b"], cfg.ln_eps)
-            x = (x.float() + ops.linear(ops.gelu(ops.linear(m, L["fc1"])), L["fc2"]).float()).to(self.dtype)
+        x = run_blocks(x, self.layers, cfg.num_heads, cfg.ln_eps)
         x = ops.layernorm(x, self.post_w, self.post_b, cfg.ln_eps)
         return ops.linear(x, self.proj)

@@ -5,9 +5,9 @@ Behaviour of the reference's OpenMiniService
 from the session's stored memory plus the request messages ("role: content"
 lines) and streams one ChatResponse per generated token, finishing with usage;
 HealthCheck reports engine state. ImageUnderstanding(-Stream) run the vision
-encoder and SpeechToText the audio encoder, then the engine, when the server was
-started with them (``vision``, ``speech``); otherwise they, and TextToSpeech (no
-vocoder), answer UNIMPLEMENTED instead of synthetic output.
+encoder and SpeechToText the audio encoder, then the engine, and TextToSpeech the
+TTS model and vocoder, when the server was started with them (``vision``,
+``speech``, ``tts``); otherwise they answer UNIMPLEMENTED instead of synthetic output.
 Session memory is kept in SQLite (the reference's database), see ``SessionStore``.
 """
 from __future__ import annotations
@@ -55,8 +55,9 @@ class SessionStore:
 
 class OpenMiniServicer:
     def __init__(self, aengine, tokenizer, store: SessionStore | None = None, metrics=None, default_max_tokens=256,
-                 vision=None, speech=None):
+                 vision=None, speech=None, tts=None):
         self.vision = vision
+        self.tts = tts
         self.speech = speech
         self.aengine = aengine
         self.tok = tokenizer
@@ -129,6 +130,18 @@ class OpenMiniServicer:
                 yield proto.SpeechToTextResponse(session_id=sid, text=piece, finished=fin, confidence=conf)
         except Exception as e:
             await context.abort(grpc.StatusCode.INVALID_ARGUMENT, f"audio: {e}")
+
+    async def TextToSpeech(self, request, context):
+        """One WAV clip streamed as byte chunks (header first); the last has finished=True."""
+        if self.tts is None:
+            await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no TTS model loaded")
+        from ..models.tts import validate_request
+        try:
+            validate_request(request.text, request.speed or 1.0, request.pitch)
+        except ValueError as e:
+            await context.abort(grpc.StatusCode.INVALID_ARGUMENT, str(e))
+        async for chunk, fin in self.tts.stream(request.text, request.voice, request.speed, request.pitch):
+            yield proto.TextToSpeechResponse(session_id=request.session_id, audio_data=chunk, finished=fin)
 
     async def _unimplemented(self, request, context):
         await context.abort(grpc.StatusCode.UNIMPLEMENTED, "this server has no vision / speech encoder loaded")

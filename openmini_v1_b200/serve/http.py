@@ -8,9 +8,9 @@ Reference-compatible surface under ``/api/v1`` (routes of
 openmini-server/src/service/http/server.rs:213-268): ``chat``,
 ``chat/stream`` (SSE), ``health``, ``models``, ``metrics``,
 ``inference/{compute,batch,stats,config,reset}``. The reference answers chat
-with placeholder strings; here every chat route runs the engine. Image /
-speech routes need encoders that this server does not load and answer 501;
-/api/v1/image/understand runs the vision encoder when one is loaded.
+with placeholder strings; here every chat route runs the engine. The image,
+speech-to-text and text-to-speech routes run their models when the server loaded
+them (/api/v1/image/understand, /api/v1/stt, /api/v1/tts) and answer 501 otherwise.
 """
 from __future__ import annotations
 
@@ -44,7 +44,7 @@ def chat_prompt(messages) -> str:
 
 
 def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metrics | None = None,
-               config=None, trainer_factory=None, vision=None, speech=None) -> FastAPI:
+               config=None, trainer_factory=None, vision=None, speech=None, tts=None) -> FastAPI:
     app = FastAPI(title="openmini_v1_b200")
     metrics = metrics or Metrics()
     metrics.model_loaded.set(1)
@@ -292,11 +292,23 @@ def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metric
             return JSONResponse({"error": f"bad audio request: {e}"}, status_code=400)
         return {"text": "".join(text), "tokens": len(text)}
 
-    for path in ("/api/v1/tts",):
-        async def _ni(path=path):
-            return JSONResponse({"error": f"{path} needs a vision / speech encoder, which is not loaded"},
-                                status_code=501)
-        app.add_api_route(path, _ni, methods=["POST"])
+    @app.post("/api/v1/tts")
+    async def tts_route(body: dict):
+        """{"text": str, "voice"?: str, "language"?: str, "speed"?: 0.25-4, "pitch"?: -20-20}
+        -> {"audio_data": base64 WAV, "sample_rate", "duration_s"}"""
+        if tts is None:
+            return JSONResponse({"error": "/api/v1/tts needs a TTS model, which is not loaded"}, status_code=501)
+        import base64
+        from ..models.tts import validate_request
+        try:
+            text, speed, pitch = str(body["text"]), float(body.get("speed", 1.0)), float(body.get("pitch", 0.0))
+            validate_request(text, speed, pitch)
+        except (KeyError, ValueError, TypeError) as e:
+            return JSONResponse({"error": f"bad tts request: {e}"}, status_code=400)
+        wav = await tts.synthesize(text, str(body.get("voice", "default")), speed, pitch)
+        sr = tts.model.cfg.sample_rate
+        return {"audio_data": base64.b64encode(wav).decode(), "sample_rate": sr,
+                "duration_s": (len(wav) - 44) / 2 / sr}
 
     from .training_api import mount_training
     mount_training(app, trainer_factory)

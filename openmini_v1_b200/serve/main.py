@@ -85,13 +85,18 @@ async def serve(args):
         if eng.device.type == "cpu":
             ac.hidden_size, ac.num_layers, ac.mlp_size, ac.num_heads = 256, 2, 512, 2
         speech = SpeechToText(aeng, tok, AudioEncoder(ac, device=eng.device, dtype=eng.model.dtype))
+    tts = None
+    if args.tts:
+        from ..models.tts import TTSModel
+        from .vision_service import TextToSpeech
+        tts = TextToSpeech(TTSModel(device=eng.device, dtype=eng.model.dtype))
     app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg, vision=vision,
-                     speech=speech)
+                     speech=speech, tts=tts)
     import uvicorn
     http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
                                          log_level="warning"))
     store = SessionStore(cfg.database.path if args.db else ":memory:")
-    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision, speech=speech),
+    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision, speech=speech, tts=tts),
                                                  f"{cfg.server.host}:{args.grpc_port or cfg.server.port}",
                                                  cfg.grpc.max_message_size_mb)
     gw = Gateway(aeng, tok, cfg.server.max_connections)
@@ -126,6 +131,8 @@ def main(argv=None):
                    help="load a vision encoder (random-init weights) and serve image understanding")
     p.add_argument("--audio", action="store_true",
                    help="load an audio encoder (random-init weights) and serve speech-to-text")
+    p.add_argument("--tts", action="store_true",
+                   help="load a text-to-speech model (random-init weights) with a Griffin-Lim vocoder")
     args = p.parse_args(argv)
     init_logging()
     asyncio.run(serve(args))

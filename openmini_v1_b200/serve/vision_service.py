@@ -93,3 +93,26 @@ class SpeechToText:
             n += 1
             lp = out.logprobs[-1] if getattr(out, "logprobs", None) else 0.0
             yield dec.push(out.new_token_ids[0]), out.finished, lp
+
+
+class TextToSpeech:
+    """Speech output: the TTS model synthesises the whole clip (off the event loop), and
+    the WAV bytes are sent in chunks whose concatenation is one WAV file (header first).
+    An empty voice is "default" and a zero speed (the protobuf default) is 1.0."""
+
+    def __init__(self, model, chunk_bytes: int = 32000):
+        self.model, self.chunk = model, chunk_bytes
+
+    @staticmethod
+    def _args(voice, speed):
+        return voice or "default", float(speed) if speed else 1.0
+
+    async def synthesize(self, text: str, voice: str = "", speed: float = 0.0, pitch: float = 0.0) -> bytes:
+        import asyncio
+        voice, speed = self._args(voice, speed)
+        return await asyncio.to_thread(self.model.synthesize_wav, text, voice, speed, float(pitch))
+
+    async def stream(self, text: str, voice: str = "", speed: float = 0.0, pitch: float = 0.0):
+        wav = await self.synthesize(text, voice, speed, pitch)
+        for i in range(0, len(wav), self.chunk):
+            yield wav[i:i + self.chunk], i + self.chunk >= len(wav)

@@ -605,3 +605,20 @@ def test_gguf_device_dequant(typ):
     got = dequantize_to_device(b.reshape(-1), typ, (4, nblk * per // 4), DEV)
     # fp32 products on both sides; a fused multiply-add may move the bf16 rounding by one step
     torch.testing.assert_close(got.float().cpu(), want.to(torch.bfloat16).float(), rtol=8e-3, atol=1e-6)
+
+
+def test_tts_acoustic_model_gpu():
+    """TTS acoustic model on the GPU kernels (GEMM, LayerNorm, GELU, bidirectional
+    FlashAttention at head_dim 128) against the same model's fp32 CPU statement with the
+    GPU's durations (rounding of a duration near .5 may differ between precisions);
+    the vocoder output is finite and as long as the durations say."""
+    from openmini_v1_b200.models.tts import TTSModel
+    g = TTSModel(device=DEV, seed=5)
+    c = TTSModel(device="cpu", dtype=torch.float32, seed=5)
+    text = "the quick brown fox"
+    _, d = g.durations(text, "v", 1.0)
+    got = g.mel(text, "v", 1.0, d=d)
+    ops.check_status()
+    _close(got.cpu(), c.mel(text, "v", 1.0, d=d.cpu()), rtol=5e-2, atol=5e-2)
+    wav = g.vocode(got)
+    assert torch.isfinite(wav).all() and wav.numel() == (int(d.sum()) - 1) * g.cfg.hop

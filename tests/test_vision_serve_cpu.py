@@ -1,7 +1,9 @@
 """Image understanding through the serving stack on CPU: image features spliced
 into the prompt through the engine match a full recompute with the same features,
 image-derived placeholder ids keep the prefix cache per image, and the HTTP and
-gRPC routes answer (501 / UNIMPLEMENTED without an encoder)."""
+gRPC routes answer (501 / UNIMPLEMENTED without an encoder). Speech in and out:
+the audio encoder, the Griffin-Lim vocoder against the speech front end, the TTS
+model's durations / voices / limits, and the TTS HTTP and gRPC routes."""
 import asyncio
 import base64
 import io
@@ -154,6 +156,95 @@ def test_audio_features_and_speech_routes(vstack):
                                         response_deserializer=proto.message("SpeechToTextResponse").FromString)
                 outs = [o async for o in call(gen())]
                 assert len(outs) == 3 and outs[-1].finished and 0 < outs[-1].confidence <= 1
+        finally:
+            await server.stop(1)
+    asyncio.run(run())
+
+
+# ----------------------------------------------------------------------------- text to speech
+
+def _small_tts():
+    from openmini_v1_b200.models.tts import TTSConfig, TTSModel
+    return TTSModel(TTSConfig(hidden_size=128, num_heads=1, mlp_size=256, gl_iters=8), dtype=torch.float32)
+
+
+def test_griffin_lim_vocoder_inverts_the_speech_front_end():
+    """log-mel of a chirp plus a tone -> vocoder -> log-mel again stays close to the
+    original (much closer than noise), and a +12 semitone shift moves a 440 Hz tone's
+    loudest band to about 880 Hz."""
+    import math
+    from openmini_v1_b200.models.audio import AudioConfig, log_mel, mel_filterbank
+    from openmini_v1_b200.models.tts import TTSConfig, TTSModel
+    m = TTSModel(TTSConfig(gl_iters=32), dtype=torch.float32)
+    ac = AudioConfig()
+    t = torch.arange(16000) / 16000
+    sig = 0.5 * torch.sin(2 * math.pi * (200 * t + 300 * t * t)) + 0.3 * torch.sin(2 * math.pi * 1200 * t)
+    lm = log_mel(sig, ac)
+    lm2 = log_mel(m.vocode(lm), ac)
+    n = min(lm.shape[0], lm2.shape[0])
+    err = float((lm[:n] - lm2[:n]).abs().mean())
+    noise = float((lm[:n] - log_mel(torch.randn(16000) * 0.1, ac)[:n]).abs().mean())
+    assert err < 0.3 and err < noise / 3, (err, noise)
+    fb = mel_filterbank(16000, 400, 80)
+    centre = (fb @ torch.linspace(0, 8000, 201)) / fb.sum(1).clamp(min=1e-9)
+    tone = log_mel(0.5 * torch.sin(2 * math.pi * 440 * t), ac)
+    up = log_mel(m.vocode(tone, pitch=12.0), ac)
+    f = float(centre[int(up.mean(0).argmax())])
+    assert 700 < f < 1050, f
+
+
+def test_tts_durations_voices_and_limits():
+    import wave
+    from openmini_v1_b200.models.tts import MAX_TEXT
+    m = _small_tts()
+    _, d1 = m.durations("hello there", speed=1.0)
+    _, d2 = m.durations("hello there", speed=2.0)
+    assert d1.numel() == len(b"hello there") and (d1 >= 1).all()
+    assert abs(int(d2.sum()) - int(d1.sum()) / 2) <= d1.numel()
+    wav = m.synthesize("hello there")
+    assert wav.numel() == (int(d1.sum()) - 1) * m.cfg.hop and torch.isfinite(wav).all()
+    a, b, c = (m.synthesize_wav("hi", voice=v) for v in ("alice", "alice", "bob"))
+    assert a == b and a != c
+    with wave.open(io.BytesIO(a)) as w:
+        assert (w.getframerate(), w.getnchannels(), w.getsampwidth()) == (16000, 1, 2) and w.getnframes() > 0
+    for bad in (dict(text=""), dict(text="x" * (MAX_TEXT + 1)), dict(text="a", speed=5.0),
+                dict(text="a", pitch=-21.0)):
+        with pytest.raises(ValueError):
+            m.synthesize(**bad)
+
+
+def test_tts_http_and_grpc_routes(vstack):
+    import wave
+    import grpc
+    from openmini_v1_b200.serve import proto
+    from openmini_v1_b200.serve.grpc_server import OpenMiniServicer, start_grpc_server
+    from openmini_v1_b200.serve.vision_service import TextToSpeech
+    aeng, tok, m, vis = vstack
+    tts = TextToSpeech(_small_tts(), chunk_bytes=4000)
+    c = TestClient(create_app(aeng, tok, "tiny", tts=tts))
+    r = c.post("/api/v1/tts", json={"text": "good morning", "voice": "v1", "speed": 1.5})
+    assert r.status_code == 200, r.text
+    wav = base64.b64decode(r.json()["audio_data"])
+    with wave.open(io.BytesIO(wav)) as w:
+        assert abs(w.getnframes() / 16000 - r.json()["duration_s"]) < 1e-6
+    assert c.post("/api/v1/tts", json={"text": ""}).status_code == 400
+    assert c.post("/api/v1/tts", json={"text": "a", "speed": 9}).status_code == 400
+    assert TestClient(create_app(aeng, tok, "tiny")).post("/api/v1/tts", json={"text": "a"}).status_code == 501
+
+    async def run():
+        server, port = await start_grpc_server(OpenMiniServicer(aeng, tok, tts=tts), "127.0.0.1:0")
+        try:
+            async with grpc.aio.insecure_channel(f"127.0.0.1:{port}") as ch:
+                call = ch.unary_stream(f"/{proto.SERVICE}/TextToSpeech",
+                                       request_serializer=proto.message("TextToSpeechRequest").SerializeToString,
+                                       response_deserializer=proto.message("TextToSpeechResponse").FromString)
+                outs = [o async for o in call(proto.TextToSpeechRequest(session_id="s", text="good morning",
+                                                                        voice="v1", speed=1.5))]
+                assert len(outs) > 1 and outs[-1].finished and not any(o.finished for o in outs[:-1])
+                assert b"".join(o.audio_data for o in outs) == wav and outs[0].session_id == "s"
+                with pytest.raises(grpc.aio.AioRpcError) as e:
+                    _ = [o async for o in call(proto.TextToSpeechRequest(text=""))]
+                assert e.value.code() == grpc.StatusCode.INVALID_ARGUMENT
         finally:
             await server.stop(1)
     asyncio.run(run())
