@@ -22,4 +22,7 @@ def dequantize_to_device(raw, typ: int, shape, device, dtype=torch.bfloat16) -> 
         out = torch.empty(n, dtype=torch.bfloat16, device=dev)
         _native.C().gguf_dequant(r, int(typ), out)
         return out.view(*shape).to(dtype)
-    return torch.from_numpy(np.ascontiguousarray(dequantize(raw, typ, n))).view(*shape).to(dtype).to(dev)
+    a = np.ascontiguousarray(dequantize(raw, typ, n))
+    if not a.flags.writeable:  # an F32 tensor is a view of the read-only file map: own a copy
+        a = a.copy()
+    return torch.from_numpy(a).view(*shape).to(dtype).to(dev)

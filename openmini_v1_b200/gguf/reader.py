@@ -65,7 +65,7 @@ class GGUFReader:
         return default
 
     def model_config(self):
-        from ..models.config import DSAConfig, ModelConfig, MoEConfig
+        from ..models.config import DSAConfig, MLAConfig, ModelConfig, MoEConfig
         D = int(self.get("embedding_length"))
         H = int(self.get("attention.head_count"))
         Hkv = int(self.get("attention.head_count_kv", H))
@@ -87,6 +87,12 @@ class GGUFReader:
             dsa.indexer_heads = int(self.get("dsa.indexer_heads", 4))
             dsa.indexer_dim = int(self.get("dsa.indexer_dim", 64))
             dsa.top_k = int(self.get("dsa.top_k", 2048))
+        mla = MLAConfig()
+        if self.get("attention.kv_lora_rank"):  # DeepSeek-style latent attention (deepseek2 keys)
+            dr = int(self.get("rope.dimension_count", 64))
+            mla = MLAConfig(enabled=True, kv_lora_rank=int(self.get("attention.kv_lora_rank")), qk_rope_dim=dr,
+                            qk_nope_dim=hd - dr, v_head_dim=int(self.get("attention.value_length", hd - dr)),
+                            q_lora_rank=int(self.get("attention.q_lora_rank", 0) or 0))
         return ModelConfig(
             name=str(self.metadata.get("general.name", self.architecture)), vocab_size=int(vocab), hidden_size=D,
             num_layers=int(self.get("block_count")), num_heads=H, num_kv_heads=Hkv, head_dim=hd,
@@ -94,4 +100,4 @@ class GGUFReader:
             rms_eps=float(self.get("attention.layer_norm_rms_epsilon", 1e-5)),
             rope_theta=float(self.get("rope.freq_base", 10000.0)),
             max_position=int(self.get("context_length", 4096)),
-            tie_embeddings="output.weight" not in self.tensors, moe=moe, dsa=dsa)
+            tie_embeddings="output.weight" not in self.tensors, moe=moe, dsa=dsa, mla=mla)

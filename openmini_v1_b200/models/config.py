@@ -52,6 +52,7 @@ class MLAConfig:
     qk_nope_dim: int = 128
     qk_rope_dim: int = 64
     v_head_dim: int = 128
+    q_lora_rank: int = 0       # > 0: q = W_qb RMSNorm(W_qa x) (low-rank query), else q = W_q x
 
 
 @dataclass

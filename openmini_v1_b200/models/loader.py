@@ -128,26 +128,10 @@ def load_gguf_model(path: str, device="cpu", par=None, weight_format="bf16", dty
     model.layers = []
     for i in range(cfg.num_layers):
         L = {"attn_norm": dense("blk.{i}.attn_norm.weight", i), "ffn_norm": dense("blk.{i}.ffn_norm.weight", i)}
-        q_rows = (r * model.hq * hd, (r + 1) * model.hq * hd)
-        kv_rows = (r * model.hkv * hd, (r + 1) * model.hkv * hd) if cfg.num_kv_heads >= tp else (0, hd)
-        # fused qkv: dequantised concatenation keeps the q|k|v row order the kernels expect
-        parts = [src.get("blk.{i}.attn_q.weight", i), src.get("blk.{i}.attn_k.weight", i),
-                 src.get("blk.{i}.attn_v.weight", i)]
-        if model.weight_format == "q4" and all(p.type == GGMLType.Q4_0 for p in parts):
-            qs, ds = [], []
-            for p, rr in zip(parts, (q_rows, kv_rows, kv_rows)):
-                qn, dn = quants.split_q4_0(p.raw, *p.shape)
-                qs.append(qn[rr[0]:rr[1]])
-                ds.append(dn[rr[0]:rr[1]])
-            L["qkv"] = Q4Weight.from_parts(torch.from_numpy(np.concatenate(qs)).to(model.device),
-                                           torch.from_numpy(np.concatenate(ds).astype(np.float32))
-                                           .to(torch.bfloat16).to(model.device))
+        if cfg.mla.enabled:
+            _load_mla(src, model, L, i)
         else:
-            w = np.concatenate([parts[0].to_numpy()[q_rows[0]:q_rows[1]], parts[1].to_numpy()[kv_rows[0]:kv_rows[1]],
-                                parts[2].to_numpy()[kv_rows[0]:kv_rows[1]]])
-            L["qkv"] = _wrap(model, torch.from_numpy(w))
-        o = src.get("blk.{i}.attn_output.weight", i)
-        L["o"] = _load_linear(src, o, model, col_slice=(r * model.hq * hd, (r + 1) * model.hq * hd))
+            _load_qkv(src, model, L, i)
         if src.find("blk.{i}.ffn_gate_inp.weight", i) is not None:
             _load_moe(src, model, L, i)
             model.layers.append(L)
@@ -161,18 +145,80 @@ def load_gguf_model(path: str, device="cpu", par=None, weight_format="bf16", dty
     return model
 
 
+def _load_qkv(src: _Src, model: DecoderLM, L: dict, i: int):
+    cfg, tp, r, hd = model.cfg, model.par.tp, model.par.tp_rank, model.cfg.head_dim
+    q_rows = (r * model.hq * hd, (r + 1) * model.hq * hd)
+    kv_rows = (r * model.hkv * hd, (r + 1) * model.hkv * hd) if cfg.num_kv_heads >= tp else (0, hd)
+    # fused qkv: dequantised concatenation keeps the q|k|v row order the kernels expect
+    parts = [src.get("blk.{i}.attn_q.weight", i), src.get("blk.{i}.attn_k.weight", i),
+             src.get("blk.{i}.attn_v.weight", i)]
+    if model.weight_format == "q4" and all(p.type == GGMLType.Q4_0 for p in parts):
+        qs, ds = [], []
+        for p, rr in zip(parts, (q_rows, kv_rows, kv_rows)):
+            qn, dn = quants.split_q4_0(p.raw, *p.shape)
+            qs.append(qn[rr[0]:rr[1]])
+            ds.append(dn[rr[0]:rr[1]])
+        L["qkv"] = Q4Weight.from_parts(torch.from_numpy(np.concatenate(qs)).to(model.device),
+                                       torch.from_numpy(np.concatenate(ds).astype(np.float32))
+                                       .to(torch.bfloat16).to(model.device))
+    else:
+        w = np.concatenate([parts[0].to_numpy()[q_rows[0]:q_rows[1]], parts[1].to_numpy()[kv_rows[0]:kv_rows[1]],
+                            parts[2].to_numpy()[kv_rows[0]:kv_rows[1]]])
+        L["qkv"] = _wrap(model, torch.from_numpy(w))
+    o = src.get("blk.{i}.attn_output.weight", i)
+    L["o"] = _load_linear(src, o, model, col_slice=(r * model.hq * hd, (r + 1) * model.hq * hd))
+
+
+def _load_mla(src: _Src, model: DecoderLM, L: dict, i: int):
+    """Latent attention of layer i from DeepSeek-style GGUF tensors:
+    attn_q [H (dn + dr), D] or attn_q_a [Rq, D] + attn_q_a_norm [Rq] + attn_q_b [H (dn + dr), Rq];
+    attn_kv_a_mqa [512 + 64, D] (latent | shared RoPE key); attn_kv_a_norm [512];
+    attn_kv_b [H (dn + dv), 512] (per head: dn key rows then dv value rows), or the split
+    attn_k_b / attn_v_b (either orientation; told apart by shape); attn_output [D, H dv].
+    Heads are split under TP; the latent projection is replicated.
+    Reference: MLAWeights of openmini-server/src/model/inference/model.rs:962-1027."""
+    cfg, m, tp, r = model.cfg, model.cfg.mla, model.par.tp, model.par.tp_rank
+    H, Hl, dn, dr, dv = cfg.num_heads, model.hq, m.qk_nope_dim, m.qk_rope_dim, m.v_head_dim
+    heads = slice(r * Hl, (r + 1) * Hl)
+    dev, dt = model.device, model.dtype
+    f = lambda name: src.get(name, i).to_numpy()  # noqa: E731
+    t = lambda a: torch.from_numpy(np.array(a, dtype=np.float32)).to(dt).to(dev)  # noqa: E731  (own copy)
+    qrows = (r * Hl * (dn + dr), (r + 1) * Hl * (dn + dr))
+    if src.find("blk.{i}.attn_q_a.weight", i) is not None:
+        L["mla_q_a"] = t(f("blk.{i}.attn_q_a.weight"))
+        L["mla_q_a_norm"] = t(f("blk.{i}.attn_q_a_norm.weight"))
+        L["mla_q_b"] = t(f("blk.{i}.attn_q_b.weight")[qrows[0]:qrows[1]])
+    else:
+        L["mla_q"] = t(f("blk.{i}.attn_q.weight")[qrows[0]:qrows[1]])
+    L["mla_dkv"] = t(f("blk.{i}.attn_kv_a_mqa.weight"))
+    L["mla_kv_norm"] = t(f("blk.{i}.attn_kv_a_norm.weight"))
+    lat = m.kv_lora_rank
+    if src.find("blk.{i}.attn_kv_b.weight", i) is not None:
+        kvb = f("blk.{i}.attn_kv_b.weight").reshape(H, dn + dv, lat)
+        uk, uv = kvb[:, :dn], kvb[:, dn:]
+    else:
+        uk = f("blk.{i}.attn_k_b.weight").reshape(H, -1)
+        uv = f("blk.{i}.attn_v_b.weight").reshape(H, -1)
+        kb, vb = src.get("blk.{i}.attn_k_b.weight", i).shape, src.get("blk.{i}.attn_v_b.weight", i).shape
+        uk = uk.reshape(H, dn, lat) if kb[-1] == lat else uk.reshape(H, lat, dn).transpose(0, 2, 1)
+        uv = uv.reshape(H, dv, lat) if vb[-1] == lat else uv.reshape(H, lat, dv).transpose(0, 2, 1)
+    L["mla_uk"], L["mla_uv"] = t(uk[heads]), t(uv[heads])
+    L["o"] = _load_linear(src, src.get("blk.{i}.attn_output.weight", i), model,
+                          col_slice=(r * Hl * dv, (r + 1) * Hl * dv))
+
+
 def _load_moe(src: _Src, model: DecoderLM, L: dict, i: int):
     """MoE FFN of layer i from llama.cpp's stacked expert tensors: ffn_gate_inp [E(+Z), D],
     ffn_{gate,up}_exps [E, Fe, D], ffn_down_exps [E, D, Fe] and the optional shared expert
     ffn_{gate,up}_shexp [Fs, D], ffn_down_shexp [D, Fs] (column / row split under TP).
     Reference: the MoE layer weights of openmini-server/src/model/inference/model.rs:813-960."""
-    L["router"] = torch.from_numpy(np.ascontiguousarray(src.get("blk.{i}.ffn_gate_inp.weight", i).to_numpy())) \
+    L["router"] = torch.from_numpy(np.array(src.get("blk.{i}.ffn_gate_inp.weight", i).to_numpy(), np.float32)) \
         .to(model.dtype).to(model.device)
     g = src.get("blk.{i}.ffn_gate_exps.weight", i).to_numpy()
     u = src.get("blk.{i}.ffn_up_exps.weight", i).to_numpy()
     d = src.get("blk.{i}.ffn_down_exps.weight", i).to_numpy()
     L["experts_gate_up"] = [_wrap(model, torch.from_numpy(np.concatenate([g[e], u[e]]))) for e in range(g.shape[0])]
-    L["experts_down"] = [_wrap(model, torch.from_numpy(np.ascontiguousarray(d[e]))) for e in range(d.shape[0])]
+    L["experts_down"] = [_wrap(model, torch.from_numpy(np.array(d[e], np.float32))) for e in range(d.shape[0])]
     if src.find("blk.{i}.ffn_gate_shexp.weight", i) is not None:
         tp, r = model.par.tp, model.par.tp_rank
         sg = src.get("blk.{i}.ffn_gate_shexp.weight", i).to_numpy()
@@ -181,7 +227,7 @@ def _load_moe(src: _Src, model: DecoderLM, L: dict, i: int):
         Fs = sg.shape[0] // tp
         L["shared_gate_up"] = _wrap(model, torch.from_numpy(np.concatenate([sg[r * Fs:(r + 1) * Fs],
                                                                             su[r * Fs:(r + 1) * Fs]])))
-        L["shared_down"] = _wrap(model, torch.from_numpy(np.ascontiguousarray(sd[:, r * Fs:(r + 1) * Fs])))
+        L["shared_down"] = _wrap(model, torch.from_numpy(np.array(sd[:, r * Fs:(r + 1) * Fs], np.float32)))
 
 
 def _wrap(model, w: torch.Tensor):
@@ -194,18 +240,27 @@ def _wrap(model, w: torch.Tensor):
 
 
 def save_gguf_model(model: DecoderLM, path: str, quant: str = "f32", tokenizer_tokens=None):
-    """Write an unsharded DecoderLM (tp = 1) as GGUF. quant: f32 | f16 | bf16 | q4_0 | q8_0 | i8 | q6_k | q5_0 | q8_k | iq4_nl."""
+    """Write an unsharded DecoderLM (tp = 1) as GGUF (architecture deepseek2 for latent
+    attention, llama otherwise). quant: f32 | f16 | bf16 | q4_0 | q8_0 | i8 | q6_k | q5_0 | q8_k
+    | iq4_nl; the latent-attention projections are written in f32."""
     cfg = model.cfg
     if model.par.tp != 1:
         raise ValueError("save an unsharded (tp=1) model")
-    w = GGUFWriter(path, "llama")
-    a = "llama."
+    arch = "deepseek2" if cfg.mla.enabled else "llama"
+    w = GGUFWriter(path, arch)
+    a = arch + "."
     for k, v in [("embedding_length", cfg.hidden_size), ("block_count", cfg.num_layers),
                  ("attention.head_count", cfg.num_heads), ("attention.head_count_kv", cfg.num_kv_heads),
                  ("feed_forward_length", cfg.intermediate_size), ("context_length", cfg.max_position),
                  ("rope.freq_base", float(cfg.rope_theta)), ("attention.layer_norm_rms_epsilon", float(cfg.rms_eps)),
                  ("vocab_size", cfg.vocab_size)]:
         w.add_kv(a + k, v)
+    if cfg.mla.enabled:
+        m = cfg.mla
+        for k, v in [("attention.kv_lora_rank", m.kv_lora_rank), ("attention.q_lora_rank", m.q_lora_rank),
+                     ("attention.key_length", m.qk_nope_dim + m.qk_rope_dim), ("attention.value_length", m.v_head_dim),
+                     ("rope.dimension_count", m.qk_rope_dim)]:
+            w.add_kv(a + k, v)
     if cfg.moe.num_experts:
         w.add_kv(a + "expert_count", cfg.moe.num_experts)
         w.add_kv(a + "expert_used_count", cfg.moe.top_k)
@@ -241,11 +296,23 @@ def save_gguf_model(model: DecoderLM, path: str, quant: str = "f32", tokenizer_t
     for i, L in enumerate(model.layers):
         w.add_tensor(f"blk.{i}.attn_norm.weight", npf(L["attn_norm"]))
         w.add_tensor(f"blk.{i}.ffn_norm.weight", npf(L["ffn_norm"]))
-        qkv = npf(L["qkv"])
-        nq, nk = cfg.num_heads * hd, cfg.num_kv_heads * hd
-        add_lin(f"blk.{i}.attn_q.weight", qkv[:nq])
-        add_lin(f"blk.{i}.attn_k.weight", qkv[nq:nq + nk])
-        add_lin(f"blk.{i}.attn_v.weight", qkv[nq + nk:])
+        if cfg.mla.enabled:
+            if "mla_q_a" in L:
+                w.add_tensor(f"blk.{i}.attn_q_a.weight", npf(L["mla_q_a"]))
+                w.add_tensor(f"blk.{i}.attn_q_a_norm.weight", npf(L["mla_q_a_norm"]))
+                w.add_tensor(f"blk.{i}.attn_q_b.weight", npf(L["mla_q_b"]))
+            else:
+                w.add_tensor(f"blk.{i}.attn_q.weight", npf(L["mla_q"]))
+            w.add_tensor(f"blk.{i}.attn_kv_a_mqa.weight", npf(L["mla_dkv"]))
+            w.add_tensor(f"blk.{i}.attn_kv_a_norm.weight", npf(L["mla_kv_norm"]))
+            kvb = np.concatenate([npf(L["mla_uk"]), npf(L["mla_uv"])], axis=1)  # [H, dn + dv, 512]
+            w.add_tensor(f"blk.{i}.attn_kv_b.weight", kvb.reshape(-1, kvb.shape[-1]))
+        else:
+            qkv = npf(L["qkv"])
+            nq, nk = cfg.num_heads * hd, cfg.num_kv_heads * hd
+            add_lin(f"blk.{i}.attn_q.weight", qkv[:nq])
+            add_lin(f"blk.{i}.attn_k.weight", qkv[nq:nq + nk])
+            add_lin(f"blk.{i}.attn_v.weight", qkv[nq + nk:])
         add_lin(f"blk.{i}.attn_output.weight", npf(L["o"]))
         if "router" in L:
             w.add_tensor(f"blk.{i}.ffn_gate_inp.weight", npf(L["router"]))

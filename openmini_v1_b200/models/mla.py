@@ -35,12 +35,26 @@ LAT, ROPE = 512, 64
 def init_mla(model, L: dict, gen, shared, std: float):
     cfg, m = model.cfg, model.cfg.mla
     D, H = cfg.hidden_size, model.hq
-    L["mla_q"] = model._randn(gen, H * (m.qk_nope_dim + m.qk_rope_dim), D, std=std)
+    if m.q_lora_rank:
+        L["mla_q_a"] = model._randn(gen, m.q_lora_rank, D, std=std)
+        L["mla_q_a_norm"] = torch.ones(m.q_lora_rank, dtype=model.dtype, device=model.device)
+        L["mla_q_b"] = model._randn(gen, H * (m.qk_nope_dim + m.qk_rope_dim), m.q_lora_rank, std=std)
+    else:
+        L["mla_q"] = model._randn(gen, H * (m.qk_nope_dim + m.qk_rope_dim), D, std=std)
     L["mla_dkv"] = model._randn(shared, LAT + ROPE, D, std=std)
     L["mla_kv_norm"] = torch.ones(LAT, dtype=model.dtype, device=model.device)
     L["mla_uk"] = model._randn(gen, H, m.qk_nope_dim, LAT, std=std * 4)
     L["mla_uv"] = model._randn(gen, H, m.v_head_dim, LAT, std=std * 4)
     L["o"] = model._randn(gen, D, H * m.v_head_dim, std=std)
+
+
+def mla_query(model, L: dict, a: torch.Tensor) -> torch.Tensor:
+    """[T, D] -> [T, H (dn + dr)]: the full query projection, or the low-rank one
+    (down-projection, RMSNorm, up-projection) when the checkpoint has it."""
+    if "mla_q_a" in L:
+        qa = ops.rmsnorm(ops.linear(a, L["mla_q_a"]), L["mla_q_a_norm"], model.cfg.rms_eps)
+        return ops.linear(qa, L["mla_q_b"])
+    return ops.linear(a, L["mla_q"])
 
 
 def mla_scale(cfg) -> float:
@@ -56,7 +70,7 @@ def mla_attention(model, i: int, L: dict, a: torch.Tensor, fb, kv) -> torch.Tens
     """a: normed hidden rows [T, D] -> attention output [T, H * dv] (before W_o)."""
     cfg, m = model.cfg, model.cfg.mla
     T, H, dn, dr = a.shape[0], model.hq, m.qk_nope_dim, m.qk_rope_dim
-    q = ops.linear(a, L["mla_q"]).view(T, H, dn + dr)
+    q = mla_query(model, L, a).view(T, H, dn + dr)
     ck = ops.linear(a, L["mla_dkv"])
     c = ops.rmsnorm(ck[:, :LAT].contiguous(), L["mla_kv_norm"], cfg.rms_eps)
     k_r = ref.rope(ck[:, LAT:].reshape(T, 1, ROPE), fb.positions, model.mla_inv_freq, cfg.rope_mode).view(T, ROPE)
@@ -75,7 +89,11 @@ def mla_reference_layer(model, L: dict, a: torch.Tensor, positions: torch.Tensor
     cfg, m = model.cfg, model.cfg.mla
     T, H, dn = a.shape[0], model.hq, m.qk_nope_dim
     f = lambda t: t.float()
-    q = (f(a) @ f(L["mla_q"]).t()).view(T, H, -1)
+    if "mla_q_a" in L:
+        qa = ref.rmsnorm(f(a) @ f(L["mla_q_a"]).t(), f(L["mla_q_a_norm"]), cfg.rms_eps).float()
+        q = (qa @ f(L["mla_q_b"]).t()).view(T, H, -1)
+    else:
+        q = (f(a) @ f(L["mla_q"]).t()).view(T, H, -1)
     ck = f(a) @ f(L["mla_dkv"]).t()
     c = ref.rmsnorm(ck[:, :LAT], f(L["mla_kv_norm"]), cfg.rms_eps).float()
     k_r = ref.rope(ck[:, LAT:].reshape(T, 1, ROPE), positions, model.mla_inv_freq, cfg.rope_mode).float()

@@ -96,7 +96,8 @@ async def serve(args):
     http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
                                          log_level="warning"))
     store = SessionStore(cfg.database.path if args.db else ":memory:")
-    grpc_server, gport = await start_grpc_server(OpenMiniServicer(aeng, tok, store, metrics, vision=vision, speech=speech, tts=tts),
+    servicer = OpenMiniServicer(aeng, tok, store, metrics, vision=vision, speech=speech, tts=tts)
+    grpc_server, gport = await start_grpc_server(servicer,
                                                  f"{cfg.server.host}:{args.grpc_port or cfg.server.port}",
                                                  cfg.grpc.max_message_size_mb)
     gw = Gateway(aeng, tok, cfg.server.max_connections)

@@ -65,3 +65,68 @@ def test_mla_decode_reference_rows():
     s = (q[1] @ rows[:17].t()) * 0.05
     assert torch.allclose(out[1], torch.softmax(s, -1) @ rows[:17, :512], atol=1e-5)
     assert torch.allclose(out[0], rows[0, :512].expand(2, 512), atol=1e-6)
+
+
+def _logits(m, T=19):
+    i32 = dict(dtype=torch.int32)
+    fb = ForwardBatch(torch.arange(3, 3 + T, **i32), torch.arange(T, **i32), torch.arange(T, **i32),
+                      torch.arange(2, **i32)[None], torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T,
+                      torch.arange(T))
+    return m.logits(m(fb, m.allocate_kv(2))).float()
+
+
+def test_mla_gguf_round_trip(tmp_path):
+    """DeepSeek-style GGUF (deepseek2 keys; attn_q or the low-rank attn_q_a / _norm / _b;
+    attn_kv_a_mqa, attn_kv_a_norm and attn_kv_b, or the split attn_k_b / attn_v_b in the
+    transposed orientation) loads into the same model: identical logits."""
+    import numpy as np
+    from openmini_v1_b200.gguf.reader import GGUFReader
+    from openmini_v1_b200.gguf.writer import GGUFWriter
+    from openmini_v1_b200.models.loader import load_gguf_model, save_gguf_model
+    for q_lora in (0, 48):
+        c = _cfg()
+        c.dtype = "float32"
+        c.mla.q_lora_rank = q_lora
+        m = DecoderLM(c, device="cpu", seed=7)
+        p = str(tmp_path / f"mla{q_lora}.gguf")
+        save_gguf_model(m, p)
+        r = GGUFReader(p)
+        assert r.architecture == "deepseek2" and ("blk.0.attn_q_a.weight" in r.tensors) == bool(q_lora)
+        got = load_gguf_model(p)
+        assert got.cfg.mla.enabled and got.cfg.mla.q_lora_rank == q_lora and got.cfg.mla.qk_nope_dim == 32
+        want = _logits(m)
+        assert (_logits(got) - want).abs().max().item() < 1e-4 * max(1.0, want.abs().max().item())
+        # the split form: attn_k_b stored [H, 512, dn] (transposed), attn_v_b [H, dv, 512]
+        p2 = str(tmp_path / f"mla{q_lora}_split.gguf")
+        w = GGUFWriter(p2, "deepseek2")
+        for k, v in r.metadata.items():
+            if k not in ("general.architecture", "general.alignment"):
+                w.add_kv(k, v)
+        H = c.num_heads
+        for name, t in r.tensors.items():
+            a = t.to_numpy()
+            if name.endswith("attn_kv_b.weight"):
+                kvb = a.reshape(H, 32 + 32, 512)
+                w.add_tensor(name.replace("kv_b", "k_b"), np.ascontiguousarray(kvb[:, :32].transpose(0, 2, 1)))
+                w.add_tensor(name.replace("kv_b", "v_b"), np.ascontiguousarray(kvb[:, 32:]))
+            else:
+                w.add_tensor(name, a)
+        w.write()
+        assert (_logits(load_gguf_model(p2)) - want).abs().max().item() < 1e-4 * max(1.0, want.abs().max().item())
+
+
+def test_mla_low_rank_query_matches_reference():
+    c = _cfg()
+    c.mla.q_lora_rank = 48
+    m = DecoderLM(c, device="cpu", seed=3)
+    T = 9
+    i32 = dict(dtype=torch.int32)
+    fb = ForwardBatch(torch.arange(T, **i32), torch.arange(T, **i32), torch.arange(T, **i32),
+                      torch.arange(1, **i32)[None], torch.zeros(T, **i32), torch.arange(1, T + 1, **i32), T,
+                      torch.tensor([T - 1]))
+    L = m.layers[0]
+    assert "mla_q_a" in L and "mla_q" not in L
+    a = torch.randn(T, c.hidden_size, generator=torch.Generator().manual_seed(1))
+    got = mla_attention(m, 0, L, a, fb, m.allocate_kv(1))
+    want = mla_reference_layer(m, L, a, fb.positions)
+    assert (got - want).abs().max().item() < 1e-4 * max(1.0, want.abs().max().item())
