@@ -5,11 +5,15 @@ row-parallel reductions and the vocabulary all-gather of the LM head (NCCL
 through torch.distributed). ``attach_tp_transport`` installs the transport a
 TP decoder runs with:
 
-* ``"symm"``: the fused kernels over symmetric peer memory -- the o-proj and
-  down-proj GEMMs store their output tiles straight into the owner rank's
-  partials slot over NVLink (GEMM -> reduce-scatter in one kernel) and the
-  reduce / residual / RMSNorm / all-gather step is one kernel
-  (:mod:`.symm`, ``csrc/comm/symm.cu``); NCCL still carries the LM-head gather.
+* ``"symm"`` (default, pull): the row-parallel GEMMs (o-proj, down-proj) write their
+  partials locally; one kernel per layer step pulls every peer's partials of its own
+  rows over NVLink, adds the residual, applies the next RMSNorm and publishes the
+  normed rows, and the next column-parallel weight-only GEMM waits for the gathered
+  rows inside the kernel (bounded flag wait) before its first TMA load
+  (:mod:`.symm`, ``csrc/comm/symm.cu``); NCCL still carries the LM-head collectives.
+* ``"symm_push"``: the row-parallel GEMMs store their output tiles straight into the
+  owner rank's partials slot over NVLink and publish the epoch themselves
+  (GEMM -> reduce-scatter in one kernel).
 * ``"nccl"``: every row-parallel output is all-reduced by NCCL (the baseline
   the fused path is measured against).
 
