@@ -47,7 +47,11 @@ class EngineConfig:
                                                              224, 256])
     eos_token_id: int | None = None
     seed: int = 0
-    speculative_k: int = 0                 # > 0: n-gram speculative decoding for greedy requests
+    speculative_k: int = 0                 # > 0: speculative decoding (greedy and sampled requests)
+    speculative_adaptive: bool = True      # per-request draft length follows the acceptance rate
+    speculative_k_min: int = 1
+    speculative_k_max: int = 0             # 0: speculative_k
+    speculative_accept_threshold: float = 0.7
     draft_engine: object = None            # with speculative_k: an LLMEngine of a draft model proposes instead
     mtp_head: object = None                # with speculative_k: a models.mtp.MTPHead or CALMChunkHead proposes
     preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)

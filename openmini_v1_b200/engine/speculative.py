@@ -1,22 +1,39 @@
 """Speculative decoding with an n-gram (prompt-lookup) proposer.
 
-For greedy requests, each decode step proposes up to ``k`` draft tokens per
-sequence by matching the sequence's last n tokens (n = n_max .. n_min) against
-its earlier history and copying what followed the most recent match. One
-forward over [last token, draft_1 .. draft_m] per sequence (KV written for
-every row into slots reserved ahead) yields the model's greedy choice after
-each prefix; the longest prefix of drafts equal to those choices is accepted
-plus the model's next token, so a step emits 1 .. m+1 tokens and the output
-is identical to plain greedy decoding. KV of rejected drafts sits in slots
-beyond the sequence length and is overwritten later.
+Each decode step proposes up to ``k`` draft tokens per sequence, by default by
+matching the sequence's last n tokens (n = n_max .. n_min) against its earlier
+history and copying what followed the most recent match. One forward over
+[last token, draft_1 .. draft_m] per sequence (KV written for every row into
+slots reserved ahead) gives the model's distribution after each prefix. KV of
+rejected drafts sits in slots beyond the sequence length and is overwritten later.
+
+* Greedy requests: the longest prefix of drafts equal to the model's argmax is
+  accepted plus the model's next token, so a step emits 1 .. m+1 tokens and the
+  output is identical to plain greedy decoding.
+* Sampled requests (temperature > 0): speculative sampling with a deterministic
+  draft (Leviathan, Kalman and Matias, "Fast inference from transformers via
+  speculative decoding", ICML 2023; Chen et al., "Accelerating large language model
+  decoding with speculative sampling", 2023). With the draft distribution a point
+  mass on d_j, draft j is accepted with probability p_j(d_j), where p_j is the
+  sampler's distribution at that row: temperature, then top-k, then top-p, the
+  kept set of ``ops.reference.sample``. At the first rejection the token is drawn
+  from p_j with d_j removed and renormalised; if every draft is accepted, a bonus
+  token is drawn from p_m. The emitted sequence has exactly the sampler's
+  distribution. The uniforms come from a generator keyed by (request seed, token
+  offset), so a run repeats, but the stream differs from the non-speculative
+  sampler's Philox stream.
+* Adaptive draft length (per request): after a step with acceptance rate a/m >=
+  ``speculative_accept_threshold`` the request's k grows by one, up to
+  ``speculative_k_max``; below half the threshold it shrinks by one, down to
+  ``speculative_k_min``.
 
 Proposers: n-gram lookup, a draft model (``DraftModelProposer``) or a
 multi-token-prediction head (``models.mtp.MTPProposer``, fed the hidden row
 behind each sequence's last emitted token after every verified step).
 
-Reference: draft / verify speculative decoding with adaptive k
-(openmini-server/src/model/inference/speculative.rs,
-speculative_decoding_v2.rs); the proposer here needs no draft model.
+Reference: draft / verify speculative decoding with adaptive draft length and
+sampled acceptance (openmini-server/src/model/inference/speculative.rs:60-110,
+503-560, speculative_decoding_v2.rs:22-57).
 """
 from __future__ import annotations
 
@@ -71,19 +88,67 @@ class DraftModelProposer:
 
 def eligible(r) -> bool:
     p = r.params
-    return (p.temperature == 0.0 and p.repetition_penalty == 1.0 and not p.logprobs and not p.return_sampling_mask
+    return (p.repetition_penalty == 1.0 and not p.logprobs and not p.return_sampling_mask
             and not p.return_routing)
 
 
+def _probs(row: torch.Tensor, p) -> torch.Tensor:
+    """The sampler's distribution over one row of logits (fp32, on the row's device)."""
+    from ..ops.reference import _cutoff_mask
+    x = row.float() / p.temperature
+    x = x - x.max()
+    keep = _cutoff_mask(x, int(p.top_k), float(p.top_p))
+    e = torch.where(keep, torch.exp(x), torch.zeros_like(x))
+    return e / e.sum()
+
+
+def _draw(prob: torch.Tensor, gen: torch.Generator) -> int:
+    return int(torch.multinomial(prob.double().cpu(), 1, generator=gen))
+
+
+def _seed(eng, r) -> int:
+    return r.params.seed if r.params.seed is not None else eng.cfg.seed * 7919 + r.seq_id
+
+
+def _verify_sampled(eng, r, dr: list, logits: torch.Tensor) -> list:
+    """Speculative sampling of one request over its verify rows (logits [m + 1, V])."""
+    gen = torch.Generator().manual_seed((_seed(eng, r) * 1000003 + r.rng_offset) & 0x7FFFFFFFFFFFFFFF)
+    u = torch.rand(len(dr), generator=gen, dtype=torch.float64).tolist()
+    out = []
+    for j, d in enumerate(dr):
+        pj = _probs(logits[j], r.params)
+        if u[j] < float(pj[d]):
+            out.append(d)
+            continue
+        pj[d] = 0.0
+        out.append(_draw(pj / pj.sum(), gen))
+        return out
+    out.append(_draw(_probs(logits[len(dr)], r.params), gen))
+    return out
+
+
+def _adapt(eng, r, proposed: int, accepted: int):
+    cfg = eng.cfg
+    if not cfg.speculative_adaptive or proposed == 0:
+        return
+    k = getattr(r, "spec_k", cfg.speculative_k)
+    rate = accepted / proposed
+    if rate >= cfg.speculative_accept_threshold:
+        k = min(k + 1, cfg.speculative_k_max or cfg.speculative_k)
+    elif rate < cfg.speculative_accept_threshold / 2:
+        k = max(k - 1, cfg.speculative_k_min)
+    r.spec_k = k
+
+
 def spec_decode_step(eng, so, proposer) -> list:
-    """One verified speculative step for a pure decode batch of greedy requests."""
+    """One verified speculative step for a pure decode batch (greedy and sampled requests)."""
     chunks = so.chunks
     rows_ids, rows_pos, rows_slot, rows_seq, rows_ctx = [], [], [], [], []
     drafts = []
     for si, c in enumerate(chunks):
         r = c.req
         p = r.num_tokens - 1
-        room = min(proposer.k, r.params.max_tokens - len(r.output_token_ids) - 1,
+        room = min(getattr(r, "spec_k", proposer.k), r.params.max_tokens - len(r.output_token_ids) - 1,
                    eng.cfg.max_model_len - r.num_tokens - 1)
         if getattr(proposer, "wants_request", False):
             d = proposer.propose(r.all_token_ids, max(room, 0), req=r)
@@ -114,7 +179,8 @@ def spec_decode_step(eng, so, proposer) -> list:
                       max_ctx=eng.cfg.max_model_len, logits_idx=torch.arange(T, device=dev))
     eng.stage.h2d_bytes = host.numel() * 4 + bt.size * 4
     x = eng.model(fb, eng.kv)
-    greedy = eng.model.logits(x).argmax(-1).to(torch.int32).cpu().tolist()
+    logits = eng.model.logits(x)
+    greedy = logits.argmax(-1).to(torch.int32).cpu().tolist()
     observe = getattr(proposer, "observe", None)
     eng.stage.d2h_bytes = T * 4
     now = time.monotonic()
@@ -124,15 +190,20 @@ def spec_decode_step(eng, so, proposer) -> list:
     eng.stats.setdefault("spec_accepted", 0)
     for c, dr in zip(chunks, drafts):
         r = c.req
-        g = greedy[o:o + len(dr) + 1]
-        a = 0
-        while a < len(dr) and dr[a] == g[a]:
-            a += 1
-        new = dr[:a] + [g[a]]
+        if r.params.temperature > 0:
+            new = _verify_sampled(eng, r, dr, logits[o:o + len(dr) + 1])
+            a = len(new) - 1
+        else:
+            g = greedy[o:o + len(dr) + 1]
+            a = 0
+            while a < len(dr) and dr[a] == g[a]:
+                a += 1
+            new = dr[:a] + [g[a]]
         last_row = o + a  # hidden row whose prediction is the last emitted token
         o += len(dr) + 1
         eng.stats["spec_proposed"] += len(dr)
         eng.stats["spec_accepted"] += a
+        _adapt(eng, r, len(dr), a)
         r.num_computed = r.num_tokens
         emitted, reason = [], None
         for t in new:
@@ -146,7 +217,7 @@ def spec_decode_step(eng, so, proposer) -> list:
             if reason:
                 break
         if observe is not None and not reason:
-            observe(r, x[last_row], g[a])
+            observe(r, x[last_row], new[-1])
         if reason:
             r.finish_reason, r.finish_time = reason, now
             eng.sched.finish(r)

@@ -191,7 +191,7 @@ def philox4x32_10(c0, c1, c2, c3, k0, k1):
 def _cutoff_mask(x, k, p):
     """Kept set for top-k then top-p over scaled, max-shifted logits x (1-D fp32)."""
     V = x.numel()
-    keep = torch.ones(V, dtype=torch.bool)
+    keep = torch.ones(V, dtype=torch.bool, device=x.device)
     if 0 < k < V:
         kth = torch.topk(x, k).values[-1]
         keep &= x >= kth
