@@ -52,6 +52,9 @@ class EngineConfig:
     speculative_k_min: int = 1
     speculative_k_max: int = 0             # 0: speculative_k
     speculative_accept_threshold: float = 0.7
+    speculative_acceptance: str = "exact"  # sampled requests: "exact" | "typical" (lossy, accepts more)
+    typical_epsilon: float = 0.09          # typical acceptance: p(x) > min(epsilon, delta exp(-H(p)))
+    typical_delta: float = 0.3
     draft_engine: object = None            # with speculative_k: an LLMEngine of a draft model proposes instead
     mtp_head: object = None                # with speculative_k: a models.mtp.MTPHead or CALMChunkHead proposes
     preemption_mode: str = "recompute"     # "recompute" | "swap" (KV kept on the host while preempted)

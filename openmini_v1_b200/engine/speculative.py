@@ -22,6 +22,11 @@ rejected drafts sits in slots beyond the sequence length and is overwritten late
   distribution. The uniforms come from a generator keyed by (request seed, token
   offset), so a run repeats, but the stream differs from the non-speculative
   sampler's Philox stream.
+* ``speculative_acceptance="typical"``: the typical-acceptance rule of Medusa (Cai et
+  al., "Medusa: simple LLM inference acceleration framework with multiple decoding
+  heads", 2024): draft j is accepted when p_j(d_j) > min(epsilon, delta exp(-H(p_j)))
+  (H the entropy of p_j); at the first rejection the token is drawn from p_j. It
+  accepts more drafts at high temperature but does not preserve the distribution.
 * Adaptive draft length (per request): after a step with acceptance rate a/m >=
   ``speculative_accept_threshold`` the request's k grows by one, up to
   ``speculative_k_max``; below half the threshold it shrinks by one, down to
@@ -37,6 +42,7 @@ sampled acceptance (openmini-server/src/model/inference/speculative.rs:60-110,
 """
 from __future__ import annotations
 
+import math
 import time
 
 import numpy as np
@@ -114,9 +120,20 @@ def _verify_sampled(eng, r, dr: list, logits: torch.Tensor) -> list:
     """Speculative sampling of one request over its verify rows (logits [m + 1, V])."""
     gen = torch.Generator().manual_seed((_seed(eng, r) * 1000003 + r.rng_offset) & 0x7FFFFFFFFFFFFFFF)
     u = torch.rand(len(dr), generator=gen, dtype=torch.float64).tolist()
+    cfg = eng.cfg
+    typical = getattr(cfg, "speculative_acceptance", "exact") == "typical"
+    if not typical and getattr(cfg, "speculative_acceptance", "exact") != "exact":
+        raise ValueError(f"unknown speculative_acceptance {cfg.speculative_acceptance!r}")
     out = []
     for j, d in enumerate(dr):
         pj = _probs(logits[j], r.params)
+        if typical:
+            ent = float(-(pj * torch.log(pj.clamp(min=1e-30))).sum())
+            if float(pj[d]) > min(cfg.typical_epsilon, cfg.typical_delta * math.exp(-ent)):
+                out.append(d)
+                continue
+            out.append(_draw(pj, gen))
+            return out
         if u[j] < float(pj[d]):
             out.append(d)
             continue

@@ -99,3 +99,30 @@ def test_adaptive_draft_length():
     e3.spec = bad3
     e3.generate([pat], sp)
     assert bad3.asked[:5] == [4] * 5
+
+
+def test_typical_acceptance_rule():
+    """Typical acceptance keeps a draft whose probability clears min(epsilon, delta e^-H)
+    and rejects one below it; on rejection the token comes from the full distribution."""
+    import math
+    logits = torch.tensor([[3.0, 2.0, 0.0, -1.0], [0.0, 0.0, 0.0, 0.0], [1.0, 0.0, 0.0, 0.0]])
+    params = SimpleNamespace(temperature=1.0, top_k=0, top_p=1.0, seed=None)
+    cfg = SimpleNamespace(seed=0, speculative_acceptance="typical", typical_epsilon=0.09, typical_delta=0.3)
+    eng = SimpleNamespace(cfg=cfg)
+    p0 = _probs(logits[0], params)
+    ent = float(-(p0 * p0.log()).sum())
+    thr = min(0.09, 0.3 * math.exp(-ent))
+    assert float(p0[1]) > thr > float(p0[3])
+    r = SimpleNamespace(params=params, seq_id=1, rng_offset=0)
+    out = _verify_sampled(eng, r, [1, 2], logits)      # p1 uniform over 4: 0.25 > min(0.09, 0.3/4)
+    assert out[:2] == [1, 2] and len(out) == 3
+    counts = torch.zeros(4)
+    for t in range(4000):
+        o = _verify_sampled(eng, SimpleNamespace(params=params, seq_id=1, rng_offset=t), [3], logits)
+        assert len(o) == 1                                # the unlikely draft is always rejected
+        counts[o[0]] += 1
+    assert (counts / 4000 - p0).abs().max() < 0.03
+    cfg.speculative_acceptance = "bogus"
+    import pytest
+    with pytest.raises(ValueError):
+        _verify_sampled(eng, r, [1], logits)
