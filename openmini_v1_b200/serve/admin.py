@@ -107,6 +107,7 @@ class AdminService:
         self.sla = SLAMonitor()
         self.hooks = {}  # "model_status", "model_reload", "sessions", "metrics", "config", "service_action"
         self.oidc = None  # serve.oidc.OIDCVerifier: bearer JWTs from an identity provider
+        self.oidc_login = None  # serve.oidc.OIDCLogin: browser login through the provider
         if bootstrap_admin and not self.store.q("SELECT 1 FROM users"):
             self.create_user(*bootstrap_admin, role="admin", actor="bootstrap")
 
@@ -213,6 +214,37 @@ class AdminService:
             if tok is None:
                 raise HTTPException(401, "bad credentials")
             return {"token": tok, "expires_in": self.ttl}
+
+        @r.get("/auth/oidc/login")
+        async def oidc_login():
+            """Redirect the browser to the identity provider (authorization-code flow, PKCE)."""
+            if self.oidc_login is None:
+                raise HTTPException(404, "OIDC login is not configured")
+            from fastapi.responses import RedirectResponse
+            url, _ = self.oidc_login.start()
+            return RedirectResponse(url, status_code=302)
+
+        @r.get("/auth/oidc/callback")
+        async def oidc_callback(code: str = "", state: str = "", error: str = ""):
+            """The provider's redirect: exchange the code, verify the ID token, issue a session token."""
+            if self.oidc_login is None:
+                raise HTTPException(404, "OIDC login is not configured")
+            if error or not code:
+                raise HTTPException(400, f"login failed at the provider: {error or 'no code'}")
+            import asyncio
+            from .oidc import OIDCError
+            try:
+                claims = await asyncio.to_thread(self.oidc_login.finish, code, state)
+            except OIDCError as e:
+                self.store.audit("oidc", "auth.fail", "", {"reason": str(e)})
+                raise HTTPException(400, str(e))
+            role = self.oidc_login.verifier.role_of(claims)
+            name = claims.get("preferred_username") or claims.get("email") or claims.get("sub", "oidc")
+            if role is None:
+                self.store.audit(name, "auth.fail", "", {"reason": "no role"})
+                raise HTTPException(403, "the identity provider grants this user no admin role")
+            self.store.audit(name, "auth.oidc", "", {"role": role})
+            return {"token": self.issue_token(name, role), "expires_in": self.ttl, "user": name, "role": role}
 
         @r.get("/auth/me")
         async def me(p: Principal = Depends(view)):

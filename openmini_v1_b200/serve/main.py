@@ -62,6 +62,33 @@ def build_engine(cfg, preset_name=None, model_path=None, device=None):
     return LLMEngine(model, ecfg), tokenizer
 
 
+def mount_admin(app, eng, cfg, args):
+    """The /admin API and console. The admin password comes from $OPENMINI_ADMIN_PASSWORD
+    (a random one is generated and logged when it is unset); with --oidc-issuer the
+    provider's bearer tokens are accepted and /admin/auth/oidc/login runs the browser
+    login (client secret from $OPENMINI_OIDC_CLIENT_SECRET)."""
+    import os
+    import secrets
+    from .admin import AdminService, AdminStore
+    pw = os.environ.get("OPENMINI_ADMIN_PASSWORD")
+    if not pw:
+        pw = secrets.token_urlsafe(12)
+        log.warning("admin user 'admin' created with password %s (set OPENMINI_ADMIN_PASSWORD)", pw)
+    svc = AdminService(store=AdminStore(args.admin_db or ":memory:"), bootstrap_admin=("admin", pw))
+    svc.hooks["model_status"] = lambda: {"name": eng.model.cfg.name, "device": str(eng.device),
+                                         "layers": eng.model.cfg.num_layers, "vocab": eng.model.cfg.vocab_size}
+    svc.hooks["config"] = lambda: {"server": vars(cfg.server), "model": eng.model.cfg.name}
+    if args.oidc_issuer:
+        from .oidc import OIDCLogin, OIDCVerifier
+        verifier = OIDCVerifier(args.oidc_issuer, args.oidc_audience or args.oidc_client_id)
+        svc.oidc = verifier
+        if args.oidc_redirect_uri:
+            svc.oidc_login = OIDCLogin.from_discovery(verifier, args.oidc_client_id, args.oidc_redirect_uri,
+                                                      client_secret=os.environ.get("OPENMINI_OIDC_CLIENT_SECRET"))
+    svc.mount(app)
+    return svc
+
+
 async def serve(args):
     cfg = load_config(args.config)
     for w in cfg.validate():
@@ -92,6 +119,8 @@ async def serve(args):
         tts = TextToSpeech(TTSModel(device=eng.device, dtype=eng.model.dtype))
     app = create_app(aeng, tok, model_name=eng.model.cfg.name, metrics=metrics, config=cfg, vision=vision,
                      speech=speech, tts=tts)
+    if args.admin:
+        mount_admin(app, eng, cfg, args)
     import uvicorn
     http = uvicorn.Server(uvicorn.Config(app, host=cfg.server.host, port=args.http_port or cfg.server.http_port,
                                          log_level="warning"))
@@ -134,6 +163,13 @@ def main(argv=None):
                    help="load an audio encoder (random-init weights) and serve speech-to-text")
     p.add_argument("--tts", action="store_true",
                    help="load a text-to-speech model (random-init weights) with a Griffin-Lim vocoder")
+    p.add_argument("--admin", action="store_true", help="serve the /admin API and console")
+    p.add_argument("--admin-db", default=None, help="SQLite file of the admin store (default: in memory)")
+    p.add_argument("--oidc-issuer", default=None, help="accept bearer tokens of this OpenID Connect issuer")
+    p.add_argument("--oidc-client-id", default="openmini")
+    p.add_argument("--oidc-audience", default=None, help="expected audience (default: the client id)")
+    p.add_argument("--oidc-redirect-uri", default=None,
+                   help="with --oidc-issuer: enable the browser login; the URL of /admin/auth/oidc/callback")
     args = p.parse_args(argv)
     init_logging()
     asyncio.run(serve(args))

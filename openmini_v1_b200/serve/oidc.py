@@ -6,14 +6,28 @@ and cached), checks issuer, audience, expiry and not-before (with ``leeway_s``),
 maps the token to an admin role: the first of ``role_claims`` present (a string or a
 list of groups) looked up in ``role_map``, else ``default_role`` (None: reject).
 
+``OIDCLogin`` is the browser login: the authorization-code flow (RFC 6749 section
+4.1) with PKCE (RFC 7636, S256) and the OpenID Connect nonce. ``start`` returns the
+provider's authorization URL with a fresh state, code challenge and nonce; ``finish``
+takes the code and state from the redirect, sends the code with its verifier to the
+token endpoint, verifies the returned ID token with ``OIDCVerifier`` and checks that its
+nonce is the one issued. Each state is single use and expires after ``state_ttl_s``.
+``from_discovery`` reads the endpoints from the issuer's
+``/.well-known/openid-configuration``. The HTTP calls go through ``http_post`` /
+``http_get`` (urllib by default), which tests replace with a fake provider.
+
 Reference counterpart: the enterprise SSO settings of openmini-admin (OAuth2 / OIDC
-login); the reference configures them, this verifies the tokens.
+login); the reference configures them, this verifies the tokens and runs the login.
 """
 from __future__ import annotations
 
 import base64
+import hashlib
 import json
+import secrets
+import threading
 import time
+import urllib.parse
 import urllib.request
 
 from cryptography.hazmat.primitives import hashes
@@ -121,3 +135,76 @@ class OIDCVerifier:
             if best:
                 return best
         return self.default_role
+
+
+def _urllib_post(url: str, form: dict) -> dict:
+    data = urllib.parse.urlencode(form).encode()
+    req = urllib.request.Request(url, data=data, headers={"Content-Type": "application/x-www-form-urlencoded",
+                                                          "Accept": "application/json"})
+    with urllib.request.urlopen(req, timeout=10) as r:
+        return json.loads(r.read())
+
+
+def _urllib_get(url: str) -> dict:
+    with urllib.request.urlopen(url, timeout=10) as r:
+        return json.loads(r.read())
+
+
+class OIDCLogin:
+    def __init__(self, verifier: OIDCVerifier, authorization_endpoint: str, token_endpoint: str, client_id: str,
+                 redirect_uri: str, client_secret: str | None = None, scope: str = "openid profile email",
+                 state_ttl_s: float = 600.0, http_post=_urllib_post, clock=time.time):
+        self.verifier, self.auth_ep, self.token_ep = verifier, authorization_endpoint, token_endpoint
+        self.client_id, self.client_secret, self.redirect_uri, self.scope = client_id, client_secret, redirect_uri, scope
+        self.ttl, self.post, self.clock = state_ttl_s, http_post, clock
+        self._pending: dict = {}  # state -> (code verifier, nonce, created)
+        self._lock = threading.Lock()
+
+    @classmethod
+    def from_discovery(cls, verifier: OIDCVerifier, client_id: str, redirect_uri: str, http_get=_urllib_get, **kw):
+        doc = http_get(verifier.issuer.rstrip("/") + "/.well-known/openid-configuration")
+        if doc.get("issuer") != verifier.issuer:
+            raise OIDCError("discovery document names another issuer")
+        if doc.get("jwks_uri") and not verifier._keys:
+            verifier.jwks_uri = doc["jwks_uri"]
+        return cls(verifier, doc["authorization_endpoint"], doc["token_endpoint"], client_id, redirect_uri, **kw)
+
+    def start(self) -> tuple:
+        """-> (authorization URL, state)."""
+        state, nonce = secrets.token_urlsafe(24), secrets.token_urlsafe(24)
+        code_verifier = secrets.token_urlsafe(48)
+        challenge = b64url_encode(hashlib.sha256(code_verifier.encode()).digest())
+        now = self.clock()
+        with self._lock:
+            for k in [k for k, v in self._pending.items() if now - v[2] > self.ttl]:
+                del self._pending[k]
+            self._pending[state] = (code_verifier, nonce, now)
+        q = {"response_type": "code", "client_id": self.client_id, "redirect_uri": self.redirect_uri,
+             "scope": self.scope, "state": state, "nonce": nonce, "code_challenge": challenge,
+             "code_challenge_method": "S256"}
+        sep = "&" if "?" in self.auth_ep else "?"
+        return self.auth_ep + sep + urllib.parse.urlencode(q), state
+
+    def finish(self, code: str, state: str) -> dict:
+        """Code and state from the provider's redirect -> verified ID-token claims."""
+        with self._lock:
+            entry = self._pending.pop(state, None)
+        if entry is None:
+            raise OIDCError("unknown or already used login state")
+        code_verifier, nonce, created = entry
+        if self.clock() - created > self.ttl:
+            raise OIDCError("login state expired")
+        form = {"grant_type": "authorization_code", "code": code, "redirect_uri": self.redirect_uri,
+                "client_id": self.client_id, "code_verifier": code_verifier}
+        if self.client_secret:
+            form["client_secret"] = self.client_secret
+        try:
+            resp = self.post(self.token_ep, form)
+        except Exception as e:
+            raise OIDCError(f"token endpoint: {e}") from e
+        if "id_token" not in resp:
+            raise OIDCError(f"token endpoint returned no id_token: {resp.get('error', resp)}")
+        claims = self.verifier.verify(resp["id_token"])
+        if claims.get("nonce") != nonce:
+            raise OIDCError("nonce mismatch")
+        return claims

@@ -132,3 +132,103 @@ def test_oidc_bearer_tokens():
         assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {t}"}).status_code == 401, claims
     forged = _jwt(rsa.generate_private_key(public_exponent=65537, key_size=2048), "RS256", good)
     assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {forged}"}).status_code == 401
+
+
+def test_oidc_browser_login_code_flow_with_pkce():
+    """Authorization-code login against a fake provider: the redirect carries state,
+    nonce and an S256 code challenge; the callback's token request carries the matching
+    verifier; the ID token's nonce must match; states are single use; a user without a
+    mapped role is refused; discovery reads the endpoints."""
+    import hashlib
+    import time
+    import urllib.parse
+    from cryptography.hazmat.primitives.asymmetric import rsa
+    from openmini_v1_b200.serve.oidc import OIDCLogin, OIDCVerifier, b64url_encode
+    rk = rsa.generate_private_key(public_exponent=65537, key_size=2048)
+    rn = rk.public_key().public_numbers()
+    b = lambda i, n: b64url_encode(i.to_bytes(n, "big"))  # noqa: E731
+    jwks = {"keys": [{"kty": "RSA", "kid": "k1", "n": b(rn.n, 256), "e": b(rn.e, 3)}]}
+    issued = {}   # code -> (challenge, nonce, groups)
+    seen = []
+
+    def provider_token(url, form):
+        seen.append((url, dict(form)))
+        challenge, nonce, groups = issued.pop(form["code"])
+        if b64url_encode(hashlib.sha256(form["code_verifier"].encode()).digest()) != challenge:
+            return {"error": "invalid_grant"}
+        claims = {"iss": "https://idp.example", "aud": "openmini", "exp": time.time() + 60, "sub": "u7",
+                  "preferred_username": "bob", "groups": groups, "nonce": nonce}
+        return {"id_token": _jwt(rk, "RS256", claims), "token_type": "Bearer"}
+
+    verifier = OIDCVerifier("https://idp.example", "openmini", jwks=jwks, role_map={"ops-team": "operator"})
+    doc = {"issuer": "https://idp.example", "authorization_endpoint": "https://idp.example/authorize",
+           "token_endpoint": "https://idp.example/token", "jwks_uri": "https://idp.example/jwks"}
+    login = OIDCLogin.from_discovery(verifier, "openmini", "https://admin.local/admin/auth/oidc/callback",
+                                     http_get=lambda url: doc, http_post=provider_token, client_secret="s3")
+    svc = AdminService(secret=b"k" * 32)
+    svc.oidc_login = login
+    app = FastAPI()
+    svc.mount(app)
+    c = TestClient(app)
+
+    def authorize(groups, nonce_override=None):
+        r = c.get("/admin/auth/oidc/login", follow_redirects=False)
+        assert r.status_code == 302
+        url = urllib.parse.urlparse(r.headers["location"])
+        q = dict(urllib.parse.parse_qsl(url.query))
+        assert url.netloc == "idp.example" and url.path == "/authorize"
+        assert q["response_type"] == "code" and q["code_challenge_method"] == "S256" and q["client_id"] == "openmini"
+        code = "c" + q["state"][:8]
+        issued[code] = (q["code_challenge"], nonce_override or q["nonce"], groups)
+        return code, q["state"]
+
+    code, state = authorize(["ops-team"])
+    r = c.get("/admin/auth/oidc/callback", params={"code": code, "state": state})
+    assert r.status_code == 200, r.text
+    assert r.json()["user"] == "bob" and r.json()["role"] == "operator"
+    assert c.get("/admin/auth/me", headers={"Authorization": f"Bearer {r.json()['token']}"}).json() == \
+        {"user": "bob", "role": "operator"}
+    assert seen[-1][0] == "https://idp.example/token" and seen[-1][1]["client_secret"] == "s3"
+    assert seen[-1][1]["grant_type"] == "authorization_code"
+    # the state was used up
+    issued["again"] = issued.get("again", ("x", "y", []))
+    assert c.get("/admin/auth/oidc/callback", params={"code": "again", "state": state}).status_code == 400
+    # a nonce that is not the issued one is refused
+    code, state = authorize(["ops-team"], nonce_override="forged")
+    assert c.get("/admin/auth/oidc/callback", params={"code": code, "state": state}).status_code == 400
+    # a user whose groups map to no role is refused
+    code, state = authorize(["eng"])
+    assert c.get("/admin/auth/oidc/callback", params={"code": code, "state": state}).status_code == 403
+    # an unknown state, and an error from the provider
+    assert c.get("/admin/auth/oidc/callback", params={"code": "x", "state": "nope"}).status_code == 400
+    assert c.get("/admin/auth/oidc/callback", params={"error": "access_denied"}).status_code == 400
+    # an expired state
+    login.ttl = -1.0
+    code, state = authorize(["ops-team"])
+    assert c.get("/admin/auth/oidc/callback", params={"code": code, "state": state}).status_code == 400
+    # not configured
+    svc2 = AdminService(secret=b"k" * 32)
+    app2 = FastAPI()
+    svc2.mount(app2)
+    assert TestClient(app2).get("/admin/auth/oidc/login", follow_redirects=False).status_code == 404
+
+
+def test_server_entry_mounts_admin(monkeypatch):
+    """``serve.main.mount_admin``: the /admin API on the server's app, with the admin
+    password from the environment and the model status hook wired."""
+    from types import SimpleNamespace
+    from openmini_v1_b200.config.settings import load_config
+    from openmini_v1_b200.serve.main import mount_admin
+    monkeypatch.setenv("OPENMINI_ADMIN_PASSWORD", "pw-123")
+    eng = SimpleNamespace(model=SimpleNamespace(cfg=SimpleNamespace(name="tiny", num_layers=2, vocab_size=512)),
+                          device="cpu")
+    args = SimpleNamespace(admin_db=None, oidc_issuer=None, oidc_client_id="openmini", oidc_audience=None,
+                           oidc_redirect_uri=None)
+    app = FastAPI()
+    mount_admin(app, eng, load_config(None), args)
+    c = TestClient(app)
+    assert c.post("/admin/auth/login", json={"username": "admin", "password": "nope"}).status_code == 401
+    tok = c.post("/admin/auth/login", json={"username": "admin", "password": "pw-123"}).json()["token"]
+    h = {"Authorization": f"Bearer {tok}"}
+    assert c.get("/admin/model", headers=h).json()["name"] == "tiny"
+    assert c.get("/admin/ui").status_code == 200
