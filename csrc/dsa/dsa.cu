@@ -199,9 +199,13 @@ __global__ void __launch_bounds__(1024) dsa_topk_kernel(const float* __restrict_
   if (threadIdx.x == 0) out_n[row] = kk;
 }
 
-// Attention of each row over its selected keys: grid (rows, Hkv), 128 threads,
+// Attention of each row over its selected keys: grid (rows, Hkv, ns), 128 threads,
 // G query heads per KV head. Keys are processed in chunks of 128 (one per
-// thread for the scores, one dim per thread for P.V).
+// thread for the scores, one dim per thread for P.V). With ns > 1 (few rows, as in
+// decode, where rows x Hkv CTAs would leave most SMs idle) split z takes an equal
+// share of whole chunks and writes its unnormalised output with its running max and
+// sum (log2 domain) to part[((row Hq + h) ns + z) (D + 2)]; dsa_attn_merge_kernel
+// combines the splits. With ns == 1 the CTA writes the output directly.
 template <int D, int G>
 __global__ void __launch_bounds__(128) dsa_attn_kernel(const __nv_bfloat16* __restrict__ q, int q_ld,
                                                        const __nv_bfloat16* __restrict__ kc,
@@ -210,14 +214,16 @@ __global__ void __launch_bounds__(128) dsa_attn_kernel(const __nv_bfloat16* __re
                                                        const int* __restrict__ row_seq, const int* __restrict__ sel,
                                                        int sel_ld, const int* __restrict__ sel_n,
                                                        __nv_bfloat16* __restrict__ out, int out_ld, float scale_log2,
-                                                       int num_blocks) {
+                                                       int num_blocks, int ns, float* __restrict__ part) {
   constexpr int NV = D / 8;
   __shared__ float qs[G][D];
   __shared__ float ps[G][128];
   __shared__ int kblk[128];
   __shared__ float alpha_s[G], m_s[G], l_s[G];
-  const int row = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
+  const int row = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const int n = sel_n[row];
+  const int per = (((n + 127) >> 7) + ns - 1) / ns * 128;  // keys of one split, whole chunks
+  const int c_begin = z * per, c_end = min(n, c_begin + per);
   const int* srow = sel + (size_t)row * sel_ld;
   const int* btr = bt + (size_t)row_seq[row] * max_blocks;
   for (int i = tid; i < G * D; i += 128)
@@ -231,8 +237,8 @@ __global__ void __launch_bounds__(128) dsa_attn_kernel(const __nv_bfloat16* __re
   for (int g = 0; g < G; ++g) o[g] = 0.f;
   __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
-  for (int c0 = 0; c0 < n; c0 += 128) {
-    const int cn = min(128, n - c0);
+  for (int c0 = c_begin; c0 < c_end; c0 += 128) {
+    const int cn = min(128, c_end - c0);
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) s[g] = -INFINITY;
@@ -293,6 +299,19 @@ __global__ void __launch_bounds__(128) dsa_attn_kernel(const __nv_bfloat16* __re
     }
     __syncthreads();
   }
+  if (ns > 1) {
+    const int Hq = gridDim.y * G;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float* pp = part + (((size_t)row * Hq + kvh * G + g) * ns + z) * (D + 2);
+      if (tid < D) pp[tid] = o[g];
+      if (tid == 0) {
+        pp[D] = m_s[g];
+        pp[D + 1] = l_s[g];
+      }
+    }
+    return;
+  }
   if (tid < D) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -300,6 +319,28 @@ __global__ void __launch_bounds__(128) dsa_attn_kernel(const __nv_bfloat16* __re
       out[(size_t)row * out_ld + (size_t)(kvh * G + g) * D + tid] = __float2bfloat16_rn(l > 0.f ? o[g] / l : 0.f);
     }
   }
+}
+
+// Combines the ns splits of dsa_attn_kernel: grid (rows, Hq), D threads.
+// out = sum_z o_z 2^(m_z - M) / sum_z l_z 2^(m_z - M), M = max_z m_z; rows with no
+// selected key (every m_z = -inf) get zeros.
+template <int D>
+__global__ void __launch_bounds__(D) dsa_attn_merge_kernel(const float* __restrict__ part, int ns,
+                                                           __nv_bfloat16* __restrict__ out, int out_ld) {
+  const int row = blockIdx.x, h = blockIdx.y, Hq = gridDim.y, tid = threadIdx.x;
+  const float* pp = part + ((size_t)row * Hq + h) * ns * (D + 2);
+  float M = -INFINITY;
+  for (int z = 0; z < ns; ++z) M = fmaxf(M, pp[(size_t)z * (D + 2) + D]);
+  float num = 0.f, den = 0.f;
+  if (M > -INFINITY) {
+    for (int z = 0; z < ns; ++z) {
+      const float* q = pp + (size_t)z * (D + 2);
+      const float w = exp2f(q[D] - M);  // 0 for an empty split (m = -inf)
+      num += w * q[tid];
+      den += w * q[D + 1];
+    }
+  }
+  out[(size_t)row * out_ld + (size_t)h * D + tid] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
 }
 
 }  // namespace om
@@ -368,14 +409,29 @@ void om_dsa_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   if (rows == 0) return;
   const int Hkv = k_cache.size(1), D = k_cache.size(3), G = Hq / Hkv;
   TORCH_CHECK(D == 128, "dsa_attention: head_dim 128");
-  dim3 grid(rows, Hkv);
+  // Split the selected keys over ns CTAs per (row, KV head) when rows x Hkv would not
+  // fill two waves of the GPU's SMs; at most one split per 128-key chunk.
+  int sms = 148;
+  {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int chunks = std::max(1, (int)((sel.size(1) + 127) / 128));
+  const int want = (2 * sms + rows * Hkv - 1) / (rows * Hkv);
+  const int ns = std::max(1, std::min(chunks, want));
+  torch::Tensor part;
+  if (ns > 1) part = torch::empty({(long)rows * Hq * ns * (D + 2)}, q.options().dtype(at::kFloat));
+  float* part_ptr = ns > 1 ? part.data_ptr<float>() : nullptr;
+  dim3 grid(rows, Hkv, ns);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto args = std::make_tuple(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (int)q.stride(0),
                               reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
                               reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), Hkv, bt.data_ptr<int>(),
                               (int)bt.size(1), row_seq.data_ptr<int>(), sel.data_ptr<int>(), (int)sel.size(1),
                               sel_n.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                              (int)out.stride(0), (float)(scale * 1.4426950408889634), (int)k_cache.size(0));
+                              (int)out.stride(0), (float)(scale * 1.4426950408889634), (int)k_cache.size(0), ns,
+                              part_ptr);
 #define OM_DSA_LAUNCH(GG)                                                                              \
   std::apply([&](auto... xs) { om::dsa_attn_kernel<128, GG><<<grid, 128, 0, st>>>(xs...); }, args); \
   break;
@@ -389,4 +445,9 @@ void om_dsa_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   }
 #undef OM_DSA_LAUNCH
   OM_LAUNCH_CHECK();
+  if (ns > 1) {
+    om::dsa_attn_merge_kernel<128><<<dim3(rows, Hq), 128, 0, st>>>(
+        part_ptr, ns, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0));
+    OM_LAUNCH_CHECK();
+  }
 }

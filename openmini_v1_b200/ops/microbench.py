@@ -186,6 +186,23 @@ def case_dsa_index_tc(rows, keys, heads=4):
     return fn, rows * keys * 4 + keys * 128, 2.0 * rows * heads * keys * 64
 
 
+def case_dsa_sparse_decode(batch, ctx, hq, hkv, k=2048, d=128):
+    """DSA sparse attention at decode: each row attends to k selected keys of its
+    ctx-token paged KV (split over CTAs when rows x KV heads would not fill the GPU)."""
+    from .. import _native
+    mb = ctx // 16
+    nb = batch * mb
+    kc, vc = _rand(nb, hkv, 16, d, std=0.5), _rand(nb, hkv, 16, d)
+    bt = torch.randperm(nb, device="cuda").to(torch.int32).view(batch, mb).contiguous()
+    rseq = torch.arange(batch, dtype=torch.int32, device="cuda")
+    sel = torch.stack([torch.randperm(ctx, device="cuda")[:k] for _ in range(batch)]).to(torch.int32)
+    n = torch.full((batch,), k, dtype=torch.int32, device="cuda")
+    q = _rand(batch, hq * d)
+    out = torch.empty(batch, hq * d, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: _native.C().dsa_attention(q, kc, vc, bt, rseq, sel, n, out, hq, 1 / math.sqrt(d))  # noqa
+    return fn, batch * k * hkv * d * 2 * 2 + q.numel() * 4, 4.0 * batch * hq * k * d
+
+
 SUITE = {
     "gemm_bf16_decode_qkv": (case_gemm, dict(m=32, n=10240, k=8192, kind="bf16")),
     "gemm_q4_decode_qkv": (case_gemm, dict(m=32, n=10240, k=8192, kind="q4")),
@@ -205,6 +222,7 @@ SUITE = {
     "sampler_topp_mask": (case_sample, dict(batch=256, vocab=128256)),
     "mla_decode": (case_mla_decode, dict(batch=32, ctx=4096, heads=128)),
     "dsa_index_tc_prefill": (case_dsa_index_tc, dict(rows=4096, keys=32768)),
+    "dsa_sparse_decode": (case_dsa_sparse_decode, dict(batch=2, ctx=32768, hq=40, hkv=8)),
 }
 
 
