@@ -85,12 +85,13 @@ class CollectiveOps:
     def all_to_all(self, t: torch.Tensor, in_splits=None, out_splits=None) -> torch.Tensor:
         if self.size == 1:
             return t
+        t = t.contiguous()  # before empty_like, so the output is dense whatever t's strides were
         if in_splits is None:
             out = torch.empty_like(t)
-            dist.all_to_all_single(out, t.contiguous(), group=self.group)
+            dist.all_to_all_single(out, t, group=self.group)
             return out
         out = torch.empty((sum(out_splits),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-        dist.all_to_all_single(out, t.contiguous(), out_splits, in_splits, group=self.group)
+        dist.all_to_all_single(out, t, out_splits, in_splits, group=self.group)
         return out
 
 
