@@ -119,6 +119,30 @@ class BenchResult:
                 lines.append(f'openmini_bench_{k}{{scenario="{self.scenario}",quantile="{q}"}} {getattr(st, q)}')
         return "\n".join(lines) + "\n"
 
+    def to_text(self) -> str:
+        """Human-readable report (the reference's HumanExporter, export.rs:190-265)."""
+        rows = [f"scenario {self.scenario}: {self.completed}/{self.requests} requests in {self.duration_s:.2f} s",
+                f"  throughput {self.throughput_tok_s:.1f} tok/s, {self.requests_per_s:.2f} req/s, "
+                f"{self.prompt_tokens} prompt + {self.output_tokens} output tokens",
+                f"  {'latency (ms)':<14}{'mean':>10}{'p50':>10}{'p95':>10}{'p99':>10}{'max':>10}"]
+        for k, label in (("ttft_ms", "TTFT"), ("tpot_ms", "TPOT"), ("e2e_ms", "end to end")):
+            st = getattr(self, k)
+            rows.append(f"  {label:<14}" + "".join(f"{getattr(st, q):>10.2f}" for q in ("mean", "p50", "p95", "p99",
+                                                                                   "max")))
+        return "\n".join(rows) + "\n"
+
+    def export_all(self, stem: str) -> list:
+        """Write <stem>.json / .csv / .prom / .txt; returns the paths
+        (the reference's export_all_formats, export.rs:284)."""
+        out = []
+        for ext, fn in (("json", self.to_json), ("csv", self.to_csv), ("prom", self.to_prometheus),
+                        ("txt", self.to_text)):
+            path = f"{stem}.{ext}"
+            with open(path, "w") as f:
+                f.write(fn())
+            out.append(path)
+        return out
+
 
 def _arrivals(sc: Scenario, gen: torch.Generator) -> list:
     n = sc.num_requests
@@ -194,7 +218,8 @@ def main(argv=None):
     ap.add_argument("--preset", default="tiny")
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--quant", default="bf16")
-    ap.add_argument("--format", default="json", choices=["json", "csv", "prometheus"])
+    ap.add_argument("--format", default="json", choices=["json", "csv", "prometheus", "text"])
+    ap.add_argument("--export", default=None, help="also write every format to <stem>.{json,csv,prom,txt}")
     ap.add_argument("--baseline", default=None, help="JSON of a previous run: exit 1 on regression")
     ap.add_argument("--tolerance", type=float, default=0.10)
     a = ap.parse_args(argv)
@@ -204,7 +229,9 @@ def main(argv=None):
     eng = LLMEngine(m, EngineConfig(max_num_seqs=max(4, sc.num_requests),
                                     max_model_len=sc.prompt_len[1] + sc.output_len + 16))
     res = run_scenario(eng, sc, cfg.vocab_size)
-    print({"json": res.to_json, "csv": res.to_csv, "prometheus": res.to_prometheus}[a.format]())
+    print({"json": res.to_json, "csv": res.to_csv, "prometheus": res.to_prometheus, "text": res.to_text}[a.format]())
+    if a.export:
+        res.export_all(a.export)
     if a.baseline:
         with open(a.baseline) as f:
             fails = check_regression(res, json.load(f), a.tolerance)

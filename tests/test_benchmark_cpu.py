@@ -30,4 +30,11 @@ def test_run_scenarios_and_regression():
     worse = dict(j, throughput_tok_s=j["throughput_tok_s"] * 2)
     assert any("throughput" in f for f in check_regression(res, worse))
     assert "ttft_ms_p99" in res.to_csv() and 'quantile="p50"' in res.to_prometheus()
+    txt = res.to_text()
+    assert "scenario t: 6/6 requests" in txt and "TTFT" in txt and "p99" in txt
+    import tempfile, os
+    with tempfile.TemporaryDirectory() as d:
+        paths = res.export_all(os.path.join(d, "run"))
+        assert [p.rsplit(".", 1)[1] for p in paths] == ["json", "csv", "prom", "txt"]
+        assert json.load(open(paths[0]))["completed"] == 6
     assert {"short", "medium", "long", "ultra", "multi_user", "burst"} <= set(SCENARIOS)
