@@ -60,6 +60,22 @@ class _LRU:
     def __len__(self):
         return len(self.d)
 
+    def save_file(self, path: str):
+        """Write the entries (oldest first) with torch.save; a rollout worker's caches
+        can then be replayed by a trainer in another process."""
+        with self.lock:
+            items = list(self.d.items())
+        torch.save({"format": "openmini-replay-cache", "version": 1, "items": items}, path)
+
+    def load_file(self, path: str) -> int:
+        """Add the entries of a file written by ``save_file``; returns how many."""
+        blob = torch.load(path, map_location="cpu", weights_only=True)
+        if blob.get("format") != "openmini-replay-cache":
+            raise ValueError(f"{path} is not a replay cache file")
+        for k, v in blob["items"]:
+            self.put(k, v)
+        return len(blob["items"])
+
 
 class KeepRouting:
     """Per-sample router decisions: {layer: expert ids int32 [T, k]}."""
@@ -92,6 +108,12 @@ class KeepRouting:
     def clear(self):
         self.cache.clear()
 
+    def save_file(self, path: str):
+        self.cache.save_file(path)
+
+    def load_file(self, path: str) -> int:
+        return self.cache.load_file(path)
+
 
 class KeepSamplingMask:
     """Per-sample kept sets: packed int32 bit words [n_sampled, ceil(V/32)] and valid lengths."""
@@ -115,6 +137,12 @@ class KeepSamplingMask:
 
     def clear(self):
         self.cache.clear()
+
+    def save_file(self, path: str):
+        self.cache.save_file(path)
+
+    def load_file(self, path: str) -> int:
+        return self.cache.load_file(path)
 
 
 def unpack_words(words: torch.Tensor, V: int) -> torch.Tensor:

@@ -1,6 +1,7 @@
 """GRPO on CPU with a small MoE policy: advantage / KL / clip math, rollout
 through the engine with routing + sampling-mask capture, replay consistency,
 and a parameter update that moves the reward in the right direction."""
+import pytest
 import torch
 
 from openmini_v1_b200.engine.engine import EngineConfig, LLMEngine
@@ -47,6 +48,19 @@ def test_replay_caches():
     km.save("x", words)
     out = km.apply("x", torch.zeros(1, 3))
     assert torch.isinf(out[0, 1]) and out[0, 0] == 0 and out[0, 2] == 0
+    # file round trip (rollout worker -> trainer process)
+    import os
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        kr.save_file(os.path.join(d, "r.pt"))
+        km.save_file(os.path.join(d, "m.pt"))
+        kr2, km2 = KeepRouting(4, EnforceMode.STRICT), KeepSamplingMask()
+        assert kr2.load_file(os.path.join(d, "r.pt")) == 2 and km2.load_file(os.path.join(d, "m.pt")) == 1
+        assert kr2.apply_routing("c", n_tokens=1)[0].tolist() == [[0, 1]]
+        assert torch.equal(km2.apply("x", torch.zeros(1, 3)), out)
+        torch.save({"x": 1}, os.path.join(d, "bad.pt"))
+        with pytest.raises(ValueError):
+            kr2.load_file(os.path.join(d, "bad.pt"))
 
 
 def test_rollout_replay_and_update():
