@@ -120,6 +120,33 @@ class VisionEncoder:
         return [self.encode(p) for p in preprocess(images, self.cfg)]
 
 
+def pan_scan_layout(width: int, height: int, base_size: int = 896, overlap: int = 14) -> list:
+    """Tiles (x, y, w, h) covering an image: one tile when it fits in base_size x
+    base_size, else a grid of base_size windows stepped by base_size - overlap (edge
+    tiles are cut at the border). Reference: calculate_patch_layout of
+    openmini-server/src/model/inference/vision/pan_scan.rs:39-82."""
+    if width <= base_size and height <= base_size:
+        return [(0, 0, width, height)]
+    step = max(1, base_size - overlap)
+    return [(x, y, min(base_size, width - x), min(base_size, height - y))
+            for y in range(0, height, step) for x in range(0, width, step)]
+
+
+def pan_and_scan(image, cfg: "VisionConfig", base_size: int = 896, overlap: int = 14, max_tokens: int = 16384,
+                 include_global: bool = True) -> list:
+    """[H, W, 3] image -> list of crops [h, w, 3] to encode: the whole image first (when
+    ``include_global`` and it is tiled), then the tiles of ``pan_scan_layout`` in row
+    order, stopping before the encoder tokens (``cfg.num_patches`` per crop) would pass
+    ``max_tokens``. Each crop is resized to the encoder's input by ``preprocess``."""
+    x = torch.as_tensor(image)
+    H, W = int(x.shape[0]), int(x.shape[1])
+    tiles = pan_scan_layout(W, H, base_size, overlap)
+    crops = [x] if include_global and len(tiles) > 1 else []
+    crops += [x[ty:ty + th, tx:tx + tw] for tx, ty, tw, th in tiles]
+    keep = max(1, max_tokens // cfg.num_patches)
+    return crops[:keep]
+
+
 def splice_image(prompt_ids: list, image_token_id: int, num_patches: int) -> tuple:
     """Expand the single ``image_token_id`` of a prompt into ``num_patches`` placeholder
     positions. Returns (ids, rows): the rows whose embeddings the image features replace."""

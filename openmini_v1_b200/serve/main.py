@@ -103,7 +103,8 @@ async def serve(args):
         vc = VisionConfig(lm_hidden=eng.model.cfg.hidden_size)
         if eng.device.type == "cpu":
             vc.hidden_size, vc.num_layers, vc.mlp_size, vc.num_heads = 256, 2, 512, 2
-        vision = ImageUnderstanding(aeng, tok, VisionEncoder(vc, device=eng.device, dtype=eng.model.dtype))
+        vision = ImageUnderstanding(aeng, tok, VisionEncoder(vc, device=eng.device, dtype=eng.model.dtype),
+                                    pan_scan=args.pan_scan)
     speech = None
     if args.audio:
         from ..models.audio import AudioConfig, AudioEncoder
@@ -159,6 +160,7 @@ def main(argv=None):
     p.add_argument("--db", action="store_true", help="persist chat sessions to [database].path")
     p.add_argument("--vision", action="store_true",
                    help="load a vision encoder (random-init weights) and serve image understanding")
+    p.add_argument("--pan-scan", action="store_true", help="with --vision: tile large images (pan and scan)")
     p.add_argument("--audio", action="store_true",
                    help="load an audio encoder (random-init weights) and serve speech-to-text")
     p.add_argument("--tts", action="store_true",

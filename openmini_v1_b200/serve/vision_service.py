@@ -36,15 +36,26 @@ def image_ids(data: bytes, n: int, vocab: int, reserved: int = 256) -> list:
 
 
 class ImageUnderstanding:
-    def __init__(self, aengine, tokenizer, encoder, default_max_tokens: int = 256):
+    """``pan_scan``: large images are tiled (``models.vision.pan_and_scan``: the whole
+    image plus base_size tiles) and the features of every crop are spliced in order."""
+
+    def __init__(self, aengine, tokenizer, encoder, default_max_tokens: int = 256, pan_scan: bool = False,
+                 pan_scan_base: int = 896, pan_scan_max_tokens: int = 16384):
         self.aengine, self.tok, self.enc = aengine, tokenizer, encoder
         self.default_max = default_max_tokens
         self.vocab = aengine.engine.model.cfg.vocab_size
+        self.pan_scan, self.ps_base, self.ps_max = pan_scan, pan_scan_base, pan_scan_max_tokens
 
     def prepare(self, image_bytes: bytes, question: str):
         """-> (prompt ids, (first image position, features [P, hidden]))."""
         img = decode_image(image_bytes)
-        feats = self.enc(img)[0]
+        if self.pan_scan:
+            import torch
+            from ..models.vision import pan_and_scan
+            crops = pan_and_scan(img, self.enc.cfg, self.ps_base, max_tokens=self.ps_max)
+            feats = torch.cat([self.enc(c)[0] for c in crops])
+        else:
+            feats = self.enc(img)[0]
         P = feats.shape[0]
         head = self.tok.encode("user: <image>\n")
         tail = self.tok.encode(f"{question}\nassistant:", add_bos=False)

@@ -248,3 +248,28 @@ def test_tts_http_and_grpc_routes(vstack):
         finally:
             await server.stop(1)
     asyncio.run(run())
+
+
+def test_pan_and_scan_tiles_large_images(vstack):
+    from openmini_v1_b200.models.vision import pan_and_scan, pan_scan_layout
+    assert pan_scan_layout(800, 600) == [(0, 0, 800, 600)]
+    tiles = pan_scan_layout(2000, 900, base_size=896, overlap=14)
+    assert len(tiles) == 3 * 2 and tiles[1] == (882, 0, 896, 896) and tiles[2] == (1764, 0, 236, 896)
+    covered = np.zeros((900, 2000), dtype=bool)
+    for x, y, w, h in tiles:
+        covered[y:y + h, x:x + w] = True
+    assert covered.all()
+    aeng, tok, m, vis = vstack
+    cfg = vis.enc.cfg
+    img = np.random.default_rng(5).integers(0, 255, (60, 130, 3), dtype=np.uint8)
+    crops = pan_and_scan(img, cfg, base_size=48, overlap=4)
+    assert crops[0].shape == (60, 130, 3) and len(crops) == 1 + 3 * 2
+    assert len(pan_and_scan(img, cfg, base_size=48, overlap=4, max_tokens=3 * cfg.num_patches)) == 3
+    b = io.BytesIO()
+    np.save(b, img)
+    ps = ImageUnderstanding(aeng, tok, vis.enc, default_max_tokens=2, pan_scan=True, pan_scan_base=48,
+                            pan_scan_max_tokens=4 * cfg.num_patches)
+    ids, (pos, feats) = ps.prepare(b.getvalue(), "what?")
+    assert feats.shape[0] == 4 * cfg.num_patches and len(ids) > feats.shape[0]
+    text, pt, n = asyncio.run(ps.answer(b.getvalue(), "what?"))
+    assert n == 2 and pt == len(ids)
