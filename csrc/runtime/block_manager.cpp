@@ -103,13 +103,17 @@ class BlockManager {
     return cached;
   }
 
-  bool can_append(int64_t sid, int n) const {
+  // Free blocks that appending n tokens takes: new blocks plus a copy of a shared,
+  // partly filled last block (copy-on-write).
+  int append_need(int64_t sid, int n) const {
     const Seq& s = get(sid);
     const int need = blocks_needed((int)s.tokens.size() + n) - (int)s.blocks.size();
     int cow = 0;
     if (!s.blocks.empty() && (s.tokens.size() % bs_) != 0 && ref_[s.blocks.back()] > 1) cow = 1;
-    return need + cow <= num_free();
+    return std::max(need, 0) + cow;
   }
+
+  bool can_append(int64_t sid, int n) const { return append_need(sid, n) <= num_free(); }
 
   // Append tokens to a sequence. Returns copy-on-write pairs (src, dst) that
   // the caller must apply to the device cache before writing new KV.
@@ -304,6 +308,7 @@ void bind_block_manager(py::module_& m) {
       .def("can_allocate", &BlockManager::can_allocate)
       .def("allocate", &BlockManager::allocate)
       .def("can_append", &BlockManager::can_append)
+      .def("append_need", &BlockManager::append_need)
       .def("append", &BlockManager::append)
       .def("reserve", &BlockManager::reserve)
       .def("fork", &BlockManager::fork)

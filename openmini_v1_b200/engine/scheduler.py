@@ -139,18 +139,23 @@ class Scheduler:
         # 3) decode every running request (one token each)
         decode = [r for r in self.running if not r.in_prefill]
         gone = set()  # preempted this step (requests hash by identity)
+        held = {}     # request -> free blocks its append this step takes (reserved cumulatively)
         for r in decode:
             if r in gone:
                 continue
-            while not self.bm.can_append(r.seq_id, 1):
+            need = self.bm.append_need(r.seq_id, 1)
+            while need > self.bm.num_free() - sum(held.values()):
                 v = self._victim(r)
                 if v is None:
                     break
                 self._preempt(v, out)
                 gone.add(v)
-            if not self.bm.can_append(r.seq_id, 1):
+                held.pop(v, None)
+            if need > self.bm.num_free() - sum(held.values()):
                 self._preempt(r, out)
                 gone.add(r)
+            else:
+                held[r] = need
         if gone:
             decode = [r for r in decode if r not in gone]
         for r in decode:
