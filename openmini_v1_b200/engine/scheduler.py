@@ -140,22 +140,28 @@ class Scheduler:
         decode = [r for r in self.running if not r.in_prefill]
         gone = set()  # preempted this step (requests hash by identity)
         held = {}     # request -> free blocks its append this step takes (reserved cumulatively)
+        used = 0      # sum of held
+        free = self.bm.num_free()
         for r in decode:
             if r in gone:
                 continue
             need = self.bm.append_need(r.seq_id, 1)
-            while need > self.bm.num_free() - sum(held.values()):
-                v = self._victim(r)
-                if v is None:
-                    break
-                self._preempt(v, out)
-                gone.add(v)
-                held.pop(v, None)
-            if need > self.bm.num_free() - sum(held.values()):
-                self._preempt(r, out)
-                gone.add(r)
-            else:
-                held[r] = need
+            if need > free - used:
+                while need > free - used:
+                    v = self._victim(r)
+                    if v is None:
+                        break
+                    self._preempt(v, out)
+                    gone.add(v)
+                    used -= held.pop(v, 0)
+                    free = self.bm.num_free()
+                if need > free - used:
+                    self._preempt(r, out)
+                    gone.add(r)
+                    free = self.bm.num_free()
+                    continue
+            held[r] = need
+            used += need
         if gone:
             decode = [r for r in decode if r not in gone]
         for r in decode:
