@@ -10,6 +10,7 @@ memory_leak_test.rs and concurrent_stress_test.rs, as real engine work):
 import asyncio
 import random
 
+import pytest
 import torch
 
 from openmini_v1_b200.engine.async_engine import AsyncLLMEngine
@@ -19,15 +20,17 @@ from openmini_v1_b200.models.config import tiny
 from openmini_v1_b200.models.llama import DecoderLM
 
 
-def _engine(num_blocks=None, prefix=True):
+def _engine(num_blocks=None, prefix=True, **kw):
     m = DecoderLM(tiny(), device="cpu", seed=11)
     cfg = EngineConfig(max_num_seqs=6, max_model_len=160, enable_prefix_cache=prefix, use_cuda_graph=False,
-                       num_blocks=num_blocks)
+                       num_blocks=num_blocks, **kw)
     return LLMEngine(m, cfg)
 
 
-def test_churn_with_aborts_and_preemption_frees_every_block():
-    eng = _engine(num_blocks=14)
+@pytest.mark.parametrize("kw", [{}, {"preemption_mode": "swap"}, {"speculative_k": 3}],
+                         ids=["recompute", "swap", "speculative"])
+def test_churn_with_aborts_and_preemption_frees_every_block(kw):
+    eng = _engine(num_blocks=14, **kw)
     free0 = eng.bm.num_free()
     rng = random.Random(3)
     shared = [rng.randrange(300, 30000) for _ in range(40)]
