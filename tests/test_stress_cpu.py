@@ -85,3 +85,39 @@ def test_concurrent_async_streams_with_cancellation():
         assert not eng.requests and eng.bm.num_free() == free0
     finally:
         aeng.shutdown()
+
+
+def test_http_completions_under_concurrent_clients():
+    """24 clients at once through the HTTP API (plain and SSE streaming): every answer
+    has the requested length and the engine ends with nothing in flight."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from fastapi.testclient import TestClient
+
+    from openmini_v1_b200.engine.tokenizer import ByteTokenizer
+    from openmini_v1_b200.serve.http import create_app
+    eng = _engine()
+    free0 = eng.bm.num_free()
+    aeng = AsyncLLMEngine(eng)
+    try:
+        with TestClient(create_app(aeng, ByteTokenizer(), "tiny")) as c:
+            def call(i):
+                body = {"prompt": [300 + i, 301 + i, 302 + i] * (1 + i % 3), "max_tokens": 4 + i % 4,
+                        "temperature": 0.0, "ignore_eos": True}
+                if i % 2:
+                    r = c.post("/v1/completions", json=dict(body, stream=True))
+                    events = [ln for ln in r.text.splitlines() if ln.startswith("data: ") and ln != "data: [DONE]"]
+                    return r.status_code, len(events)
+                r = c.post("/v1/completions", json=body)
+                return r.status_code, r.json()["usage"]["completion_tokens"]
+            with ThreadPoolExecutor(12) as ex:
+                res = list(ex.map(call, range(24)))
+        assert res == [(200, 4 + i % 4) for i in range(24)], res
+        import time
+        for _ in range(200):
+            if not eng.requests:
+                break
+            time.sleep(0.01)
+        assert not eng.requests and eng.bm.num_free() == free0
+    finally:
+        aeng.shutdown()
