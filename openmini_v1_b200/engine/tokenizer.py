@@ -53,6 +53,8 @@ class ByteTokenizer:
 
 
 class GGUFTokenizer:
+    dummy_prefix = True  # encode() prepends the SentencePiece space marker
+
     def __init__(self, tokens, scores=None, token_types=None, merges=None, bos_id=1, eos_id=2, unk_id=0):
         self.tokens = list(tokens)
         self.vocab_size = len(self.tokens)
@@ -162,25 +164,35 @@ class GGUFTokenizer:
 
 
 class IncrementalDecoder:
-    """Streams text from token ids without splitting multi-byte UTF-8 characters."""
+    """Streams text from token ids without splitting multi-byte UTF-8 characters. For a
+    tokenizer that prepends a dummy space (``dummy_prefix``), the first character of the
+    stream is dropped when it is that space, as ``decode`` does for the whole text."""
 
     def __init__(self, tok):
         self.tok = tok
         self.buf = b""
+        self._strip = bool(getattr(tok, "dummy_prefix", False))
+
+    def _emit(self, s: str) -> str:
+        if self._strip and s:
+            self._strip = False
+            if s[0] == " ":
+                return s[1:]
+        return s
 
     def push(self, token_id: int) -> str:
         self.buf += self.tok.decode_token(token_id)
         try:
             s = self.buf.decode("utf-8")
             self.buf = b""
-            return s
+            return self._emit(s)
         except UnicodeDecodeError as e:
             if e.start > 0:
                 s = self.buf[:e.start].decode("utf-8")
                 self.buf = self.buf[e.start:]
-                return s
+                return self._emit(s)
             if len(self.buf) > 4:  # not a truncated character: emit replacement
                 s = self.buf.decode("utf-8", errors="replace")
                 self.buf = b""
-                return s
+                return self._emit(s)
             return ""
