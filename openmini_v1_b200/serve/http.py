@@ -46,6 +46,14 @@ def chat_prompt(messages) -> str:
 def create_app(aengine, tokenizer, model_name: str = "openmini", metrics: Metrics | None = None,
                config=None, trainer_factory=None, vision=None, speech=None, tts=None) -> FastAPI:
     app = FastAPI(title="openmini_v1_b200")
+
+    async def _bad_request(request, exc):
+        # a request body with fields of the wrong type or shape (for example max_tokens: [])
+        # fails while being read into engine parameters: that is the client's error
+        return JSONResponse({"error": f"bad request: {type(exc).__name__}: {exc}"}, status_code=400)
+
+    for exc_type in (TypeError, ValueError, KeyError, AttributeError, IndexError):
+        app.add_exception_handler(exc_type, _bad_request)
     metrics = metrics or Metrics()
     metrics.model_loaded.set(1)
     started = time.time()
