@@ -1,7 +1,8 @@
 """Greedy outputs do not depend on scheduling (hypothesis over prompt sets): the
 same requests give the same tokens with whole or chunked prefill under any token
-budget, with the prefix cache on or off, and under a KV pool small enough to force
-preemption (recompute or swap) -- as one request at a time with plenty of memory."""
+budget, with the prefix cache on or off, under a KV pool small enough to force
+preemption (recompute or swap), and with n-gram speculative decoding (also under KV
+pressure) -- as one request at a time with plenty of memory."""
 import random
 
 from hypothesis import given, settings
@@ -34,6 +35,7 @@ def test_greedy_outputs_independent_of_scheduling(seed, n):
     want = [_run([p], [o], max_num_seqs=1, enable_prefix_cache=False)[0][0] for p, o in zip(prompts, outs)]
     for kw in ({}, {"max_num_batched_tokens": 7}, {"enable_chunked_prefill": False},
                {"enable_prefix_cache": False}, {"num_blocks": 10}, {"num_blocks": 10, "preemption_mode": "swap"},
-               {"num_blocks": 10, "max_num_batched_tokens": 16}):
+               {"num_blocks": 10, "max_num_batched_tokens": 16}, {"speculative_k": 3},
+               {"speculative_k": 4, "num_blocks": 10}):
         got, stats = _run(prompts, outs, **kw)
         assert got == want, kw
