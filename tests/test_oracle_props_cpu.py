@@ -64,3 +64,36 @@ def test_norm_rope_act_oracles(seed, T, D):
     half = ref.rope(xr, pos, inv, 1).float()                 # pairs (i, i + D/2)
     a, b = xr[..., : D // 2], xr[..., D // 2:]
     assert torch.allclose(half, torch.cat([a * c - b * s_, a * s_ + b * c], -1), atol=1e-4)
+
+
+@settings(max_examples=30, deadline=None)
+@given(seed=st.integers(0, 10 ** 6), k=st.integers(1, 80))
+def test_dsa_oracles(seed, k):
+    """Top-k keeps the k largest visible scores; sparse attention over every visible key
+    equals dense paged attention."""
+    from openmini_v1_b200.models import dsa
+    g = torch.Generator().manual_seed(seed)
+    lens = [int(torch.randint(1, 70, (1,), generator=g)) for _ in range(2)]
+    S, mb = 2, 5
+    nb = S * mb
+    bt = torch.randperm(nb, generator=g).view(S, mb).to(torch.int32)
+    kc = torch.randn(nb, 2, 16, 64, generator=g)
+    vc = torch.randn(nb, 2, 16, 64, generator=g)
+    rseq = torch.arange(S, dtype=torch.int32)
+    rctx = torch.tensor(lens, dtype=torch.int32)
+    scores = torch.randn(S, 80, generator=g)
+    sel, n = dsa.topk_ref(scores, rctx, k)
+    for r in range(S):
+        c = lens[r]
+        assert int(n[r]) == min(k, c)
+        chosen = set(sel[r, :int(n[r])].tolist())
+        assert all(0 <= j < c for j in chosen) and len(chosen) == int(n[r])
+        if int(n[r]) < c:
+            worst = min(float(scores[r, j]) for j in chosen)
+            rest = [float(scores[r, j]) for j in range(c) if j not in chosen]
+            assert worst >= max(rest)
+    q = torch.randn(S, 4 * 64, generator=g)
+    allk = torch.stack([torch.cat([torch.arange(c), torch.full((80 - c,), -1)]) for c in lens]).to(torch.int32)
+    sp = dsa.sparse_attention_ref(q, kc, vc, bt, rseq, allk, rctx, 4, 0.125)
+    dense = ref.paged_attention(q.view(S, 4, 64), kc, vc, bt, rseq, rctx, 4, 0.125)
+    assert torch.allclose(sp.float().view(S, 4, 64), dense.float(), atol=1e-5)
