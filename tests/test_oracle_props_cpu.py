@@ -97,3 +97,23 @@ def test_dsa_oracles(seed, k):
     sp = dsa.sparse_attention_ref(q, kc, vc, bt, rseq, allk, rctx, 4, 0.125)
     dense = ref.paged_attention(q.view(S, 4, 64), kc, vc, bt, rseq, rctx, 4, 0.125)
     assert torch.allclose(sp.float().view(S, 4, 64), dense.float(), atol=1e-5)
+
+
+@settings(max_examples=40, deadline=None)
+@given(seed=st.integers(0, 10 ** 6), N=st.integers(1, 6), KB=st.integers(1, 4), mag=st.floats(1e-3, 50.0))
+def test_weight_quantiser_error_bounds(seed, N, KB, mag):
+    """4-bit blocks of 32 (scale = block max / -8): every value within one scale step
+    (half a step except the clamped +8 end), and within bf16 rounding of the output;
+    INT8 per row (scale = row max / 127): within half a step."""
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(N, 32 * KB, generator=g) * mag).bfloat16()
+    q, d = ref.quantize_q4(w)
+    back = ref.dequant_q4(q, d).float()
+    wf = w.float()
+    step = d.float().abs().repeat_interleave(32, 1)
+    assert bool((back - wf).abs().le(step * 1.001 + back.abs() * 2 ** -8 + 1e-30).all())
+    half = (back - wf).abs() <= step * 0.501 + back.abs() * 2 ** -8 + 1e-30
+    assert half.float().mean() > 0.95
+    qi, s = ref.quantize_int8(w)
+    bi = ref.dequant_int8(qi, s).float()
+    assert bool((bi - wf).abs().le(s[:, None] * 0.501 + bi.abs() * 2 ** -8 + 1e-30).all())
