@@ -225,6 +225,65 @@ class ServerConfig:
     def to_dict(self):
         return dataclasses.asdict(self)
 
+    def to_toml(self) -> str:
+        """The whole configuration as TOML that ``from_str`` reads back to an equal object
+        (unknown keys kept in ``extra`` are written at the top level)."""
+        d = self.to_dict()
+        extra = d.pop("extra", {})
+        return _toml_table(extra, []) + "".join(_toml_table(v, [k]) for k, v in d.items())
+
+
+def _toml_key(k: str) -> str:
+    return k if k and all(c.isalnum() or c in "-_" for c in k) else _toml_str(k)
+
+
+def _toml_str(s: str) -> str:
+    out = ['"']
+    for ch in s:
+        if ch in '"\\':
+            out.append("\\" + ch)
+        elif ord(ch) < 0x20 or ord(ch) == 0x7F:
+            out.append(f"\\u{ord(ch):04x}")
+        else:
+            out.append(ch)
+    return "".join(out) + '"'
+
+
+def _toml_value(v) -> str:
+    if isinstance(v, bool):
+        return "true" if v else "false"
+    if isinstance(v, int):
+        return str(v)
+    if isinstance(v, float):
+        if v != v:
+            return "nan"
+        if v in (float("inf"), float("-inf")):
+            return "inf" if v > 0 else "-inf"
+        return repr(v)
+    if isinstance(v, str):
+        return _toml_str(v)
+    if isinstance(v, (list, tuple)):
+        return "[" + ", ".join(_toml_value(x) for x in v) + "]"
+    if isinstance(v, dict):
+        return "{" + ", ".join(f"{_toml_key(k)} = {_toml_value(x)}" for k, x in v.items()) + "}"
+    if v is None:
+        raise ValueError("TOML has no null value")
+    raise TypeError(f"cannot write {type(v).__name__} as TOML")
+
+
+def _toml_table(d: dict, path: list) -> str:
+    tables = [(k, v) for k, v in d.items() if isinstance(v, dict) and v]
+    scalars = [(k, v) for k, v in d.items() if not (isinstance(v, dict) and v)]
+    out = []
+    if path and (scalars or not tables):
+        out.append("[" + ".".join(_toml_key(p) for p in path) + "]\n")
+    out += [f"{_toml_key(k)} = {_toml_value(v)}\n" for k, v in scalars if v is not None]
+    if out:
+        out.append("\n")
+    for k, v in tables:
+        out.append(_toml_table(v, path + [k]))
+    return "".join(out)
+
 
 def _coerce(v: str, typ):
     if typ is bool:

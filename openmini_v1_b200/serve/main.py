@@ -172,7 +172,12 @@ def main(argv=None):
     p.add_argument("--oidc-audience", default=None, help="expected audience (default: the client id)")
     p.add_argument("--oidc-redirect-uri", default=None,
                    help="with --oidc-issuer: enable the browser login; the URL of /admin/auth/oidc/callback")
+    p.add_argument("--dump-config", action="store_true",
+                   help="print the effective configuration (file, defaults and OPENMINI__ overrides) as TOML")
     args = p.parse_args(argv)
+    if args.dump_config:
+        print(load_config(args.config).to_toml(), end="")
+        return
     init_logging()
     asyncio.run(serve(args))
 
