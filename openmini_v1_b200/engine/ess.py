@@ -172,8 +172,10 @@ class ElasticStorage:
 
     # ------------------------------------------------------------------ API
     def put(self, key, t: torch.Tensor):
-        self.remove(key)
         n = self._nbytes(t)
+        if n > self.dev_budget and n > self.host_budget:
+            raise ValueError(f"entry of {n} bytes is larger than either tier")
+        self.remove(key)
         if n > self.dev_budget:  # too large for the device tier: host only
             self._make_room_host(n)
             self.host[key] = self._to_host(t)
@@ -198,14 +200,19 @@ class ElasticStorage:
             out = self.dev[key]
         elif key in self.host:
             self.stats.host_hits += 1
-            self._promote(key)
-            out = self.dev[key]
+            if self._nbytes(self.host[key]) > self.dev_budget:
+                # larger than the device tier: served as a temporary device copy, kept on the host
+                self.pol_host.touch(key)
+                out = self._to_device(self.host[key])
+            else:
+                self._promote(key)
+                out = self.dev[key]
         else:
             self.stats.misses += 1
             out = None
         if self.prefetcher is not None and isinstance(key, int):
             for p in self.prefetcher.access(key):
-                if p in self.host:
+                if p in self.host and self._nbytes(self.host[p]) <= self.dev_budget:
                     self._promote(p)
                     self.stats.prefetches += 1
         return out
